@@ -1,0 +1,586 @@
+// gemm_tcgen05.cu -- dense GEMM C = A * B on B200 5th-gen tensor cores.
+//
+// Replaces the reference's mfma_gemm_lowp_kernel / mfma_gemm_highp_kernel
+// (src/teamredbench/native/kernels/mfu_gemm_lowp.hip.hpp:134-334,
+// mfu_gemm_highp.hip.hpp:39-218) and, for result semantics, the torch path's
+// torch.mm(a, b, out=out) (src/teamredbench/benchmarks/mfu.py:229-234).
+//
+// Design (one kernel template for all five input types):
+//  * persistent grid, one 192-thread CTA per SM, static tile schedule with
+//    grouped rasterisation (GROUP_M m-blocks share each B column panel in L2);
+//  * CTA tile 128 x 256, K staged 128 bytes at a time (64 bf16/f16, 32 tf32,
+//    128 e4m3/int8), 4-stage shared-memory ring fed by TMA (no multicast);
+//  * warp 0: TMA producer; warp 1: a single thread issues tcgen05.mma
+//    (cta_group::1, M=128, N=256, K=32 bytes per instruction) into a TMEM
+//    accumulator; warps 2-5: epilogue (tcgen05.ld -> convert -> global store);
+//  * two 256-column TMEM accumulators (512 columns) so the epilogue of tile i
+//    overlaps the main loop of tile i+1;
+//  * A is row-major (K-major operand, 128B swizzle); B is row-major K x N,
+//    i.e. an MN-major operand, consumed directly through the MN-major 128B
+//    swizzle layout (no re-layout pass: the reference needed an untimed
+//    pack_b_tiles_kernel, mfu_gemm_lowp.hip.hpp:82-132, this kernel does not);
+//  * every mbarrier wait is bounded (trb::kWaitTimeoutNs); a wait that gives
+//    up records a code in g_gemm_error, raises a CTA-wide abort flag, drains
+//    its own in-flight TMA / MMA work and frees TMEM before returning.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "trb_common.cuh"
+
+namespace trb {
+namespace gemm {
+
+__device__ int g_gemm_error;
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBKBytes = 128;       // K bytes per stage: one 128-byte swizzle row
+constexpr int kInstrKBytes = 32;    // K bytes consumed by one tcgen05.mma
+constexpr int kKSteps = kBKBytes / kInstrKBytes;
+constexpr int kStages = 4;
+constexpr int kAStage = kBM * kBKBytes;  // 16 KiB
+constexpr int kBStage = kBN * kBKBytes;  // 32 KiB
+constexpr int kNumAcc = 2;
+constexpr int kTmemCols = kNumAcc * kBN;  // 512
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;
+constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBStage) + 1024;  // + alignment slack
+
+// Instruction descriptor (kind::f16 / tf32 / f8f6f4 / i8): D format, A/B formats,
+// A K-major (bit 15 = 0), B MN-major (bit 16 = 1), N >> 3 at [17,23), M >> 4 at [24,29).
+constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt) {
+    return (c_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | (0u << 15) | (1u << 16) |
+           ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+// Per-input-type traits.  kind: 0 f16, 1 tf32, 2 f8f6f4, 3 i8.
+// B (MN-major) smem layout: 128-byte swizzle with 16-byte atoms (descriptor
+// layout type 2, 8-row period, SBO = 1024) for 8/16-bit types; tf32 MN-major
+// operands only exist in the 128-byte swizzle with 32-byte atoms (layout type
+// 1, 4-row period, SBO = 512), loaded with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+struct BLayout16 {
+    static constexpr uint32_t kLayoutType = 2, kSbo = 1024;
+    static constexpr CUtensorMapSwizzle kTmaSwizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+};
+struct BLayout32 {
+    static constexpr uint32_t kLayoutType = 1, kSbo = 512;
+    static constexpr CUtensorMapSwizzle kTmaSwizzle = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+};
+
+template <int DT>
+struct Traits;
+template <>
+struct Traits<TRB_BFLOAT16> {
+    using BLayout = BLayout16;
+    static constexpr int kEsize = 2, kKind = 0;
+    static constexpr uint32_t kIdesc = make_idesc(1, 1, 1);  // F32 <- BF16 x BF16
+};
+template <>
+struct Traits<TRB_FLOAT16> {
+    using BLayout = BLayout16;
+    static constexpr int kEsize = 2, kKind = 0;
+    static constexpr uint32_t kIdesc = make_idesc(1, 0, 0);  // F32 <- F16 x F16
+};
+template <>
+struct Traits<TRB_TFLOAT32> {
+    using BLayout = BLayout32;
+    static constexpr int kEsize = 4, kKind = 1;
+    static constexpr uint32_t kIdesc = make_idesc(1, 2, 2);  // F32 <- TF32 x TF32
+};
+template <>
+struct Traits<TRB_FLOAT8_E4M3FN> {
+    using BLayout = BLayout16;
+    static constexpr int kEsize = 1, kKind = 2;
+    static constexpr uint32_t kIdesc = make_idesc(1, 0, 0);  // F32 <- E4M3 x E4M3
+};
+template <>
+struct Traits<TRB_INT8> {
+    using BLayout = BLayout16;
+    static constexpr int kEsize = 1, kKind = 3;
+    static constexpr uint32_t kIdesc = make_idesc(2, 1, 1);  // S32 <- S8 x S8
+};
+
+// Shared-memory matrix descriptor, sm100 version (bit 46), swizzled layout
+// type at [61,64) (2 = 128B swizzle, 1 = 128B swizzle with 32B atoms).
+// Addresses and offsets are in 16-byte units.
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                               uint32_t layout_type = 2) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)layout_type << 61;
+    return d;
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if constexpr (KIND == 0) mma_f16(d, a, b, idesc, acc);
+    else if constexpr (KIND == 1) mma_tf32(d, a, b, idesc, acc);
+    else if constexpr (KIND == 2) mma_f8f6f4(d, a, b, idesc, acc);
+    else mma_i8(d, a, b, idesc, acc);
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+    const int group = kGroupM * num_n;
+    const int g = tile / group;
+    const int first_m = g * kGroupM;
+    const int gm = min(num_m - first_m, kGroupM);
+    const int local = tile - g * group;
+    mb = first_m + local % gm;
+    nb = local / gm;
+}
+
+// Convert 32 accumulator words of one row and store them at C[row, col .. col+31].
+template <int DT>
+__device__ __forceinline__ void store_chunk(void* C, int row, int col, int N, const uint32_t (&r)[32],
+                                            float out_scale) {
+    const bool full = col + 32 <= N;
+    if constexpr (DT == TRB_BFLOAT16 || DT == TRB_FLOAT8_E4M3FN || DT == TRB_FLOAT16) {
+        uint16_t* out = static_cast<uint16_t*>(C) + (size_t)row * N + col;
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float lo = __uint_as_float(r[2 * i]), hi = __uint_as_float(r[2 * i + 1]);
+            if constexpr (DT == TRB_FLOAT8_E4M3FN) {
+                lo *= out_scale;
+                hi *= out_scale;
+            }
+            if constexpr (DT == TRB_FLOAT16) {
+                __half2 h = __floats2half2_rn(lo, hi);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+                __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+        }
+        if (full) {
+            uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col + i < N) out[i] = (uint16_t)(w[i >> 1] >> ((i & 1) * 16));
+        }
+    } else {  // tf32 -> f32, int8 -> s32: raw 32-bit words
+        uint32_t* out = static_cast<uint32_t*>(C) + (size_t)row * N + col;
+        if (full) {
+            uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col + i < N) out[i] = r[i];
+        }
+    }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        void* __restrict__ C, int M, int N, int K, float out_scale) {
+    using Tr = Traits<DT>;
+    constexpr int kBKElems = kBKBytes / Tr::kEsize;         // K elements per stage
+    constexpr int kBoxN = 128 / Tr::kEsize;                 // N elements per B box (one swizzle row)
+    constexpr int kBBoxes = kBN / kBoxN;                    // B boxes per stage
+    constexpr int kBBoxBytes = kBKElems * 128;              // bytes of one B box == MN-atom stride (LBO)
+    constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;  // K rows of B per instruction
+
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kStages];
+    __shared__ __align__(8) uint64_t empty_bar[kStages];
+    __shared__ __align__(8) uint64_t accf_bar[kNumAcc];
+    __shared__ __align__(8) uint64_t acce_bar[kNumAcc];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+
+    const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    const uint32_t sA = smem_base;
+    const uint32_t sB = smem_base + kStages * kAStage;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_m = (M + kBM - 1) / kBM;
+    const int num_n = (N + kBN - 1) / kBN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + kBKElems - 1) / kBKElems;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        for (int a = 0; a < kNumAcc; ++a) {
+            mbar_init(smem_u32(&accf_bar[a]), 1);
+            mbar_init(smem_u32(&acce_bar[a]), 4);  // one arrival per epilogue warp
+        }
+        mbar_init(smem_u32(&drain_bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;  // per stage: a load is outstanding / its parity
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                int mb, nb;
+                tile_coords(tile, num_m, num_n, mb, nb);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrProducerWait);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = smem_u32(&full_bar[stage]);
+                    mbar_arrive_expect_tx(fb, kAStage + kBStage);
+                    tma_load_2d(sA + stage * kAStage, &tmA, fb, kb * kBKElems, mb * kBM);
+#pragma unroll
+                    for (int j = 0; j < kBBoxes; ++j)
+                        tma_load_2d(sB + stage * kBStage + j * kBBoxBytes, &tmB, fb, nb * kBN + j * kBoxN,
+                                    kb * kBKElems);
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: the CTA must not exit while a TMA write into its smem is pending.
+            for (int s = 0; s < kStages; ++s)
+                if (issued_mask & (1u << s))
+                    if (!mbar_wait(smem_u32(&full_bar[s]), (issued_phase >> s) & 1u, nullptr))
+                        atomicCAS(&g_gemm_error, 0, kErrDrainWait);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer (single thread)
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            int t_local = 0;
+            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++t_local) {
+                const int acc = t_local & 1;
+                const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
+                if (!mbar_wait(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
+                    atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                    abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = sA + stage * kAStage;
+                    const uint32_t b_base = sB + stage * kBStage;
+#pragma unroll
+                    for (int ks = 0; ks < kKSteps; ++ks) {
+                        const uint64_t a_desc = make_sdesc(a_base + ks * kInstrKBytes, 16, 1024);
+                        const uint64_t b_desc = make_sdesc(b_base + ks * kInstrKRows * 128, kBBoxBytes,
+                                                           Tr::BLayout::kSbo, Tr::BLayout::kLayoutType);
+                        mma<Tr::kKind>(d_tmem, a_desc, b_desc, Tr::kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(smem_u32(&empty_bar[stage]));  // frees the smem stage when these MMAs finish
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok) tc_commit(smem_u32(&accf_bar[acc]));  // accumulator complete -> epilogue
+            }
+            // Drain: all MMAs of this thread complete before TMEM is released.
+            tc_commit(smem_u32(&drain_bar));
+            if (!mbar_wait(smem_u32(&drain_bar), 0, nullptr)) atomicCAS(&g_gemm_error, 0, kErrDrainWait);
+        }
+    } else {
+        // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        int t_local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t_local) {
+            int mb, nb;
+            tile_coords(tile, num_m, num_n, mb, nb);
+            const int acc = t_local & 1;
+            const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
+            bool ok = mbar_wait(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int grow = mb * kBM + row_in_tile;
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+                tmem_wait_ld();
+                const int gcol = nb * kBN + c * 32;
+                if (grow < M && gcol < N) store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+static int encode_2d(CUtensorMap* map, const void* base, int esize, uint64_t inner, uint64_t outer,
+                     uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (fn == nullptr) {
+        set_error("cuTensorMapEncodeTiled entry point unavailable");
+        return TRB_ERR_CUDA;
+    }
+    const CUtensorMapDataType dt = esize == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * (uint64_t)esize};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d) for %llux%llu box %ux%u", (int)r, (unsigned long long)inner,
+                  (unsigned long long)outer, box_inner, box_outer);
+        return TRB_ERR_CUDA;
+    }
+    return TRB_OK;
+}
+
+template <int DT>
+static int launch_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale,
+                        cudaStream_t stream, LaunchInfo* info) {
+    using Tr = Traits<DT>;
+    constexpr int es = Tr::kEsize;
+    CUtensorMap tmA, tmB;
+    int rc = encode_2d(&tmA, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TRB_OK) return rc;
+    rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
+    if (rc != TRB_OK) return rc;
+    int dev = 0;
+    TRB_CUDA(cudaGetDevice(&dev));
+    static bool attr_set[64] = {};
+    if (dev < 64 && !attr_set[dev]) {
+        TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kSmemBytes));
+        attr_set[dev] = true;
+    }
+    const int sms = device_sm_count(dev);
+    const long tiles = (long)((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+    const int grid = (int)std::max<long>(1, std::min<long>(tiles, sms));
+    gemm_tcgen05_kernel<DT><<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, c, m, n, k, out_scale);
+    TRB_CUDA(cudaGetLastError());
+    if (info) *info = {grid, kThreads};
+    return TRB_OK;
+}
+
+int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
+           cudaStream_t stream, LaunchInfo* info) {
+    if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || b == nullptr || c == nullptr) {
+        set_error("trb_gemm_launch: dimensions must be positive and pointers non-null");
+        return TRB_ERR_ARGS;
+    }
+    const size_t es = dtype_size(dtype);
+    if (!(dtype == TRB_BFLOAT16 || dtype == TRB_FLOAT16 || dtype == TRB_TFLOAT32 || dtype == TRB_FLOAT8_E4M3FN ||
+          dtype == TRB_INT8)) {
+        set_error("unsupported dtype for native MFU kernel: %s", dtype_name(dtype));
+        return TRB_SKIPPED;
+    }
+    if (((size_t)k * es) % 16 != 0 || ((size_t)n * es) % 16 != 0) {
+        set_error("trb_gemm_launch: k*elem and n*elem must be multiples of 16 bytes (k=%d n=%d elem=%zu)", k, n, es);
+        return TRB_ERR_ALIGN;
+    }
+    if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15u) !=
+        0) {
+        set_error("trb_gemm_launch: A, B and C must be 16-byte aligned");
+        return TRB_ERR_ALIGN;
+    }
+    switch (dtype) {
+        case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16>(m, n, k, a, b, c, 1.0f, stream, info);
+        case TRB_FLOAT16: return launch_typed<TRB_FLOAT16>(m, n, k, a, b, c, 1.0f, stream, info);
+        case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32>(m, n, k, a, b, c, 1.0f, stream, info);
+        case TRB_FLOAT8_E4M3FN:
+            return launch_typed<TRB_FLOAT8_E4M3FN>(m, n, k, a, b, c, scale_a * scale_b, stream, info);
+        default: return launch_typed<TRB_INT8>(m, n, k, a, b, c, 1.0f, stream, info);
+    }
+}
+
+// ------------------------------------------------------------------ inputs
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// N(0,1) / sqrt(K) by Box-Muller from a counter hash of (seed, i).
+__device__ __forceinline__ float normal_scaled(uint64_t seed, uint64_t i, float inv_sqrt_k) {
+    const uint64_t z = mix64(seed * 0xD1B54A32D192ED03ull + i);
+    const float u1 = ((float)(z >> 40) + 1.0f) * 0x1p-24f;  // (0, 1]
+    const float u2 = (float)((z >> 16) & 0xFFFFFFu) * 0x1p-24f;
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2) * inv_sqrt_k;
+}
+
+__global__ void absmax_kernel(uint64_t n, uint64_t seed, float inv_sqrt_k, unsigned int* out_bits) {
+    float m = 0.0f;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(normal_scaled(seed, i, inv_sqrt_k)));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(out_bits, __float_as_uint(m));
+}
+
+__global__ void fill_gemm_kernel(void* data, int dtype, uint64_t n, uint64_t seed, float inv_sqrt_k,
+                                 const unsigned int* absmax_bits) {
+    const float inv_scale = absmax_bits ? 448.0f / __uint_as_float(*absmax_bits) : 1.0f;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        switch (dtype) {
+            case TRB_BFLOAT16:
+                static_cast<__nv_bfloat16*>(data)[i] = __float2bfloat16_rn(normal_scaled(seed, i, inv_sqrt_k));
+                break;
+            case TRB_FLOAT16:
+                static_cast<__half*>(data)[i] = __float2half_rn(normal_scaled(seed, i, inv_sqrt_k));
+                break;
+            case TRB_TFLOAT32: {
+                uint32_t t;
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(normal_scaled(seed, i, inv_sqrt_k)));
+                static_cast<uint32_t*>(data)[i] = t;
+                break;
+            }
+            case TRB_FLOAT8_E4M3FN:
+                static_cast<__nv_fp8_storage_t*>(data)[i] =
+                    __nv_cvt_float_to_fp8(normal_scaled(seed, i, inv_sqrt_k) * inv_scale, __NV_SATFINITE, __NV_E4M3);
+                break;
+            case TRB_INT8: {
+                const uint64_t z = mix64(seed * 0xD1B54A32D192ED03ull + i);
+                static_cast<int8_t*>(data)[i] = (int8_t)((int)(z % 255ull) - 127);
+                break;
+            }
+            default: break;
+        }
+    }
+}
+
+__global__ void round_tf32_kernel(uint32_t* data, uint64_t n) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        uint32_t t;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(__uint_as_float(data[i])));
+        data[i] = t;
+    }
+}
+
+// Fills `data` (n elements) in the BASELINE distribution of `dtype`; for e4m3
+// returns the per-tensor scale absmax / 448 in *scale_out.  `absmax_scratch`
+// is one device word used by the e4m3 absmax reduction.
+int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsigned int* absmax_scratch,
+                 float* scale_out, cudaStream_t stream) {
+    int dev = 0;
+    TRB_CUDA(cudaGetDevice(&dev));
+    const int grid = device_sm_count(dev) * 8;
+    const float inv_sqrt_k = 1.0f / sqrtf((float)k);
+    *scale_out = 1.0f;
+    if (dtype == TRB_FLOAT8_E4M3FN) {
+        TRB_CUDA(cudaMemsetAsync(absmax_scratch, 0, sizeof(unsigned int), stream));
+        absmax_kernel<<<grid, 256, 0, stream>>>(n, seed, inv_sqrt_k, absmax_scratch);
+        TRB_CUDA(cudaGetLastError());
+        fill_gemm_kernel<<<grid, 256, 0, stream>>>(data, dtype, n, seed, inv_sqrt_k, absmax_scratch);
+        TRB_CUDA(cudaGetLastError());
+        unsigned int bits = 0;
+        TRB_CUDA(cudaMemcpyAsync(&bits, absmax_scratch, sizeof(bits), cudaMemcpyDeviceToHost, stream));
+        TRB_CUDA(cudaStreamSynchronize(stream));
+        float amax;
+        memcpy(&amax, &bits, 4);
+        *scale_out = amax / 448.0f;
+        return TRB_OK;
+    }
+    fill_gemm_kernel<<<grid, 256, 0, stream>>>(data, dtype, n, seed, inv_sqrt_k, nullptr);
+    TRB_CUDA(cudaGetLastError());
+    return TRB_OK;
+}
+
+int read_error(bool clear) {
+    int v = 0;
+    TRB_CUDA(cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int)));
+    if (clear) {
+        const int zero = 0;
+        TRB_CUDA(cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)));
+    }
+    return v;
+}
+
+}  // namespace gemm
+}  // namespace trb
+
+extern "C" int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a,
+                               float scale_b, void* stream) {
+    trb::clear_error();
+    return trb::gemm::launch(dtype, m, n, k, a, b, c, scale_a, scale_b, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int trb_round_tf32(void* data, uint64_t count, void* stream) {
+    trb::clear_error();
+    if (data == nullptr || count == 0) {
+        trb::set_error("trb_round_tf32: empty input");
+        return TRB_ERR_ARGS;
+    }
+    int dev = 0;
+    TRB_CUDA(cudaGetDevice(&dev));
+    trb::gemm::round_tf32_kernel<<<trb::device_sm_count(dev) * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint32_t*>(data), count);
+    TRB_CUDA(cudaGetLastError());
+    return TRB_OK;
+}

@@ -1,0 +1,471 @@
+// trb_abi.cu -- C ABI entry points of libtrb_b200.so (see include/trb_b200.h).
+//
+// trb_hbm_run / trb_gemm_run own their device memory and time `iterations`
+// back-to-back launches with CUDA events, exactly like the reference's
+// executables (src/teamredbench/native/kernels/hbm_bandwidth.hip.cpp:390-425,
+// mfu_gemm_lowp.hip.hpp:447-485).  trb_*_host take host buffers and include the
+// host<->device copies in the call.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "trb_common.cuh"
+
+namespace trb {
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_err[1024];
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+void clear_error() { g_err[0] = '\0'; }
+
+int cuda_fail(cudaError_t err, const char* what) {
+    set_error("%s failed: %s", what, cudaGetErrorString(err));
+    return TRB_ERR_CUDA;
+}
+
+size_t dtype_size(int dtype) {
+    switch (dtype) {
+        case TRB_FLOAT32: case TRB_TFLOAT32: case TRB_INT32: return 4;
+        case TRB_BFLOAT16: case TRB_FLOAT16: return 2;
+        case TRB_FLOAT64: return 8;
+        case TRB_INT8: case TRB_FLOAT8_E4M3FN: return 1;
+        default: return 0;
+    }
+}
+
+const char* dtype_name(int dtype) {
+    switch (dtype) {
+        case TRB_FLOAT32: return "float32";
+        case TRB_BFLOAT16: return "bfloat16";
+        case TRB_FLOAT16: return "float16";
+        case TRB_FLOAT64: return "float64";
+        case TRB_INT8: return "int8";
+        case TRB_FLOAT8_E4M3FN: return "float8_e4m3fn";
+        case TRB_TFLOAT32: return "tfloat32";
+        case TRB_INT32: return "int32";
+        default: return "unknown";
+    }
+}
+
+int device_sm_count(int device) {
+    static int cache[64] = {};
+    if (device >= 0 && device < 64 && cache[device] > 0) return cache[device];
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    if (device >= 0 && device < 64) cache[device] = sms;
+    return sms;
+}
+
+
+// ------------------------------------------------------------------ RAII
+struct DeviceBuffers {
+    void* p[8] = {};
+    int n = 0;
+    ~DeviceBuffers() {
+        for (int i = 0; i < n; ++i)
+            if (p[i]) cudaFree(p[i]);
+    }
+    int alloc(void** out, size_t bytes, const char* what) {
+        void* q = nullptr;
+        cudaError_t e = cudaMalloc(&q, bytes);
+        if (e != cudaSuccess) {
+            set_error("cudaMalloc(%s, %zu bytes) failed: %s", what, bytes, cudaGetErrorString(e));
+            cudaGetLastError();
+            return TRB_ERR_CUDA;
+        }
+        p[n++] = q;
+        *out = q;
+        return TRB_OK;
+    }
+};
+
+struct StreamEvents {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t start = nullptr, stop = nullptr;
+    ~StreamEvents() {
+        if (stop) cudaEventDestroy(stop);
+        if (start) cudaEventDestroy(start);
+        if (stream) cudaStreamDestroy(stream);
+    }
+    int create() {
+        TRB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        TRB_CUDA(cudaEventCreate(&start));
+        TRB_CUDA(cudaEventCreate(&stop));
+        return TRB_OK;
+    }
+};
+
+static void fill_result_common(trb_result* out, int device) {
+    memset(out, 0, sizeof(*out));
+    out->device_id = device;
+    out->sm_count = device_sm_count(device);
+}
+
+static int check_device_errors(trb_result* out) {
+    const int e1 = hbm::read_error(true);
+    const int e2 = gemm::read_error(true);
+    if (e1 < 0 || e2 < 0) return TRB_ERR_CUDA;
+    out->device_error = e1 ? e1 : e2;
+    if (out->device_error) {
+        set_error("a bounded device wait gave up (code %d)", out->device_error);
+        return TRB_ERR_DEVICE_TIMEOUT;
+    }
+    return TRB_OK;
+}
+
+static int set_device(int device) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        set_error("no CUDA device visible");
+        return TRB_ERR_NO_DEVICE;
+    }
+    if (device < 0 || device >= count) {
+        set_error("device id %d out of range (%d devices)", device, count);
+        return TRB_ERR_ARGS;
+    }
+    TRB_CUDA(cudaSetDevice(device));
+    return TRB_OK;
+}
+
+// ------------------------------------------------------------------ host-buffer pipeline state
+struct HostPipe {
+    static constexpr int kStreams = 3;
+    cudaStream_t s[kStreams] = {};
+    cudaEvent_t start = nullptr, stop = nullptr, done[kStreams] = {};
+    void* buf[kStreams][3] = {};  // src, aux, dst chunk buffers
+    size_t chunk_bytes = 0;
+    std::mutex mu;
+};
+static HostPipe g_pipes[64];
+
+static int pipe_init(HostPipe& p, size_t chunk_bytes) {
+    if (p.s[0] == nullptr) {
+        for (int i = 0; i < HostPipe::kStreams; ++i) {
+            TRB_CUDA(cudaStreamCreateWithFlags(&p.s[i], cudaStreamNonBlocking));
+            TRB_CUDA(cudaEventCreateWithFlags(&p.done[i], cudaEventDisableTiming));
+        }
+        TRB_CUDA(cudaEventCreate(&p.start));
+        TRB_CUDA(cudaEventCreate(&p.stop));
+    }
+    if (p.chunk_bytes < chunk_bytes) {
+        for (auto& row : p.buf)
+            for (auto& b : row)
+                if (b) {
+                    cudaFree(b);
+                    b = nullptr;
+                }
+        p.chunk_bytes = 0;
+        for (auto& row : p.buf)
+            for (auto& b : row) TRB_CUDA(cudaMalloc(&b, chunk_bytes));
+        p.chunk_bytes = chunk_bytes;
+    }
+    return TRB_OK;
+}
+
+}  // namespace trb
+
+using namespace trb;
+
+extern "C" int trb_abi_version(void) { return TRB_ABI_VERSION; }
+
+extern "C" const char* trb_last_error(void) { return g_err; }
+
+extern "C" int trb_device_error(int device_id, int clear) {
+    clear_error();
+    int rc = set_device(device_id);
+    if (rc != TRB_OK) return rc;
+    const int e1 = hbm::read_error(clear != 0);
+    const int e2 = gemm::read_error(clear != 0);
+    if (e1 < 0) return e1;
+    if (e2 < 0) return e2;
+    return e1 ? e1 : e2;
+}
+
+extern "C" int trb_hbm_run(const trb_hbm_args* args, trb_result* out) {
+    clear_error();
+    if (args == nullptr || out == nullptr) {
+        set_error("trb_hbm_run: null argument");
+        return TRB_ERR_ARGS;
+    }
+    if (args->warmup < 0 || args->iterations < 0) {
+        set_error("warmup and iterations must be non-negative");
+        return TRB_ERR_ARGS;
+    }
+    const size_t es = dtype_size(args->dtype);
+    const bool supported = (args->dtype == TRB_FLOAT32 || args->dtype == TRB_BFLOAT16 ||
+                            args->dtype == TRB_FLOAT16 || args->dtype == TRB_FLOAT64 ||
+                            (args->dtype == TRB_INT8 && args->mode == TRB_COPY)) &&
+                           args->mode >= TRB_COPY && args->mode <= TRB_TRIAD;
+    if (!supported) {
+        set_error("unsupported dtype or mode for native HBM kernel: %s/%d", dtype_name(args->dtype), args->mode);
+        return TRB_SKIPPED;
+    }
+    int rc = set_device(args->device_id);
+    if (rc != TRB_OK) return rc;
+    fill_result_common(out, args->device_id);
+
+    const uint64_t count = std::max<uint64_t>(1, args->size_bytes / es);
+    const size_t bytes = count * es;
+    DeviceBuffers bufs;
+    void *src = nullptr, *dst = nullptr, *aux = nullptr;
+    if ((rc = bufs.alloc(&src, bytes, "src")) != TRB_OK) return rc;
+    if ((rc = bufs.alloc(&dst, bytes, "dst")) != TRB_OK) return rc;
+    if (args->mode == TRB_TRIAD && (rc = bufs.alloc(&aux, bytes, "aux")) != TRB_OK) return rc;
+    StreamEvents se;
+    if ((rc = se.create()) != TRB_OK) return rc;
+    if ((rc = hbm::fill_uniform(src, args->dtype, count, 0, se.stream)) != TRB_OK) return rc;
+    if (aux && (rc = hbm::fill_uniform(aux, args->dtype, count, 1, se.stream)) != TRB_OK) return rc;
+    TRB_CUDA(cudaMemsetAsync(dst, 0, bytes, se.stream));
+
+    hbm::LaunchShape shape;
+    for (int i = 0; i < args->warmup; ++i) {
+        rc = hbm::launch(args->dtype, args->mode, dst, src, aux, count, args->scale, args->variant,
+                         args->blocks_per_sm, se.stream, &shape);
+        if (rc != TRB_OK) return rc;
+    }
+    TRB_CUDA(cudaStreamSynchronize(se.stream));
+    TRB_CUDA(cudaEventRecord(se.start, se.stream));
+    for (int i = 0; i < args->iterations; ++i) {
+        rc = hbm::launch(args->dtype, args->mode, dst, src, aux, count, args->scale, args->variant,
+                         args->blocks_per_sm, se.stream, &shape);
+        if (rc != TRB_OK) return rc;
+    }
+    TRB_CUDA(cudaEventRecord(se.stop, se.stream));
+    TRB_CUDA(cudaEventSynchronize(se.stop));
+    float ms = 0.f;
+    TRB_CUDA(cudaEventElapsedTime(&ms, se.start, se.stop));
+
+    const int factor = args->mode == TRB_TRIAD ? 3 : 2;
+    out->elapsed_s = (double)ms / 1000.0 / (double)std::max(args->iterations, 1);
+    out->moved_bytes = (double)factor * (double)count * (double)es;
+    out->grid = shape.grid;
+    out->block = shape.block;
+    out->blocks_per_sm = shape.blocks_per_sm;
+    out->variant = shape.variant;
+    out->launches = shape.variant == TRB_HBM_MEMCPY ? 0 : args->iterations;
+    snprintf(out->implementation, sizeof(out->implementation), "%s", shape.impl);
+    return check_device_errors(out);
+}
+
+extern "C" int trb_hbm_host(int dtype, int mode, void* dst_host, const void* src_host, const void* aux_host,
+                            uint64_t count, double scale, int device_id, trb_result* out) {
+    clear_error();
+    if (out == nullptr || dst_host == nullptr || src_host == nullptr || count == 0 ||
+        (mode == TRB_TRIAD && aux_host == nullptr)) {
+        set_error("trb_hbm_host: null argument or empty count");
+        return TRB_ERR_ARGS;
+    }
+    const size_t es = dtype_size(dtype);
+    if (es == 0) {
+        set_error("unsupported dtype %d", dtype);
+        return TRB_SKIPPED;
+    }
+    int rc = set_device(device_id);
+    if (rc != TRB_OK) return rc;
+    if (device_id >= 64) {
+        set_error("device id too large");
+        return TRB_ERR_ARGS;
+    }
+    fill_result_common(out, device_id);
+    HostPipe& p = g_pipes[device_id];
+    std::lock_guard<std::mutex> lock(p.mu);
+    const size_t chunk_bytes = 64ull << 20;  // 64 MiB per array per chunk
+    if ((rc = pipe_init(p, chunk_bytes)) != TRB_OK) return rc;
+    const uint64_t chunk_elems = chunk_bytes / es;
+    const uint64_t nchunks = (count + chunk_elems - 1) / chunk_elems;
+
+    TRB_CUDA(cudaEventRecord(p.start, p.s[0]));
+    for (int i = 1; i < HostPipe::kStreams; ++i) TRB_CUDA(cudaStreamWaitEvent(p.s[i], p.start, 0));
+    hbm::LaunchShape shape;
+    const char* sh = static_cast<const char*>(src_host);
+    const char* ah = static_cast<const char*>(aux_host);
+    char* dh = static_cast<char*>(dst_host);
+    for (uint64_t c = 0; c < nchunks; ++c) {
+        const int si = (int)(c % HostPipe::kStreams);
+        cudaStream_t st = p.s[si];
+        const uint64_t first = c * chunk_elems;
+        const uint64_t n = std::min<uint64_t>(chunk_elems, count - first);
+        const size_t off = first * es, nb = n * es;
+        TRB_CUDA(cudaMemcpyAsync(p.buf[si][0], sh + off, nb, cudaMemcpyHostToDevice, st));
+        if (mode == TRB_TRIAD) TRB_CUDA(cudaMemcpyAsync(p.buf[si][1], ah + off, nb, cudaMemcpyHostToDevice, st));
+        rc = hbm::launch(dtype, mode, p.buf[si][2], p.buf[si][0], p.buf[si][1], n, scale, TRB_HBM_AUTO, 0, st, &shape);
+        if (rc != TRB_OK) return rc;
+        TRB_CUDA(cudaMemcpyAsync(dh + off, p.buf[si][2], nb, cudaMemcpyDeviceToHost, st));
+    }
+    for (int i = 1; i < HostPipe::kStreams; ++i) {
+        TRB_CUDA(cudaEventRecord(p.done[i], p.s[i]));
+        TRB_CUDA(cudaStreamWaitEvent(p.s[0], p.done[i], 0));
+    }
+    TRB_CUDA(cudaEventRecord(p.stop, p.s[0]));
+    TRB_CUDA(cudaEventSynchronize(p.stop));
+    float ms = 0.f;
+    TRB_CUDA(cudaEventElapsedTime(&ms, p.start, p.stop));
+    const int factor = mode == TRB_TRIAD ? 3 : 2;
+    out->elapsed_s = ms / 1000.0;
+    out->moved_bytes = (double)factor * (double)count * (double)es;
+    out->h2d_bytes = (double)count * (double)es * (mode == TRB_TRIAD ? 2.0 : 1.0);
+    out->d2h_bytes = (double)count * (double)es;
+    out->grid = shape.grid;
+    out->block = shape.block;
+    out->variant = shape.variant;
+    out->launches = (int)nchunks;
+    snprintf(out->implementation, sizeof(out->implementation), "%s+pipelined_copies", shape.impl);
+    return check_device_errors(out);
+}
+
+static bool gemm_dtype_supported(int dtype) {
+    return dtype == TRB_BFLOAT16 || dtype == TRB_FLOAT16 || dtype == TRB_TFLOAT32 || dtype == TRB_FLOAT8_E4M3FN ||
+           dtype == TRB_INT8;
+}
+
+static size_t gemm_out_size(int dtype) {
+    return (dtype == TRB_TFLOAT32 || dtype == TRB_INT8) ? 4 : 2;
+}
+
+extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
+    clear_error();
+    if (args == nullptr || out == nullptr) {
+        set_error("trb_gemm_run: null argument");
+        return TRB_ERR_ARGS;
+    }
+    if (args->m <= 0 || args->n <= 0 || args->k <= 0) {
+        set_error("matrix dimensions must be positive");
+        return TRB_ERR_ARGS;
+    }
+    if (args->warmup < 0 || args->iterations < 0) {
+        set_error("warmup and iterations must be non-negative");
+        return TRB_ERR_ARGS;
+    }
+    if (!gemm_dtype_supported(args->dtype)) {
+        set_error("unsupported dtype for native MFU kernel: %s", dtype_name(args->dtype));
+        return TRB_SKIPPED;
+    }
+    int rc = set_device(args->device_id);
+    if (rc != TRB_OK) return rc;
+    fill_result_common(out, args->device_id);
+    const size_t es = dtype_size(args->dtype);
+    const size_t m = args->m, n = args->n, k = args->k;
+    DeviceBuffers bufs;
+    void *a = nullptr, *b = nullptr, *c = nullptr, *scratch = nullptr;
+    if ((rc = bufs.alloc(&a, m * k * es, "A")) != TRB_OK) return rc;
+    if ((rc = bufs.alloc(&b, k * n * es, "B")) != TRB_OK) return rc;
+    if ((rc = bufs.alloc(&c, m * n * gemm_out_size(args->dtype), "C")) != TRB_OK) return rc;
+    if ((rc = bufs.alloc(&scratch, 256, "absmax")) != TRB_OK) return rc;
+    StreamEvents se;
+    if ((rc = se.create()) != TRB_OK) return rc;
+    float sa = 1.f, sb = 1.f;
+    rc = gemm::fill_operand(a, args->dtype, m * k, args->k, 0, static_cast<unsigned int*>(scratch), &sa, se.stream);
+    if (rc != TRB_OK) return rc;
+    rc = gemm::fill_operand(b, args->dtype, k * n, args->k, 1, static_cast<unsigned int*>(scratch), &sb, se.stream);
+    if (rc != TRB_OK) return rc;
+    TRB_CUDA(cudaMemsetAsync(c, 0, m * n * gemm_out_size(args->dtype), se.stream));
+
+    gemm::LaunchInfo info;
+    for (int i = 0; i < args->warmup; ++i) {
+        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, se.stream, &info);
+        if (rc != TRB_OK) return rc;
+    }
+    TRB_CUDA(cudaStreamSynchronize(se.stream));
+    TRB_CUDA(cudaEventRecord(se.start, se.stream));
+    for (int i = 0; i < args->iterations; ++i) {
+        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, se.stream, &info);
+        if (rc != TRB_OK) return rc;
+    }
+    TRB_CUDA(cudaEventRecord(se.stop, se.stream));
+    TRB_CUDA(cudaEventSynchronize(se.stop));
+    float ms = 0.f;
+    TRB_CUDA(cudaEventElapsedTime(&ms, se.start, se.stop));
+    out->elapsed_s = (double)ms / 1000.0 / (double)std::max(args->iterations, 1);
+    out->achieved_ops = 2.0 * (double)m * (double)n * (double)k;
+    out->grid = info.grid;
+    out->block = info.block;
+    out->blocks_per_sm = 1;
+    out->launches = args->iterations;
+    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_tma_ws_128x256");
+    return check_device_errors(out);
+}
+
+namespace trb {
+struct GemmHostState {
+    void* buf[3] = {};
+    size_t cap[3] = {};
+    cudaStream_t s = nullptr;
+    cudaEvent_t start = nullptr, stop = nullptr;
+    std::mutex mu;
+};
+static GemmHostState g_gemm_host[64];
+
+static int ensure(GemmHostState& st, int i, size_t bytes) {
+    if (st.cap[i] >= bytes) return TRB_OK;
+    if (st.buf[i]) cudaFree(st.buf[i]);
+    st.buf[i] = nullptr;
+    st.cap[i] = 0;
+    TRB_CUDA(cudaMalloc(&st.buf[i], bytes));
+    st.cap[i] = bytes;
+    return TRB_OK;
+}
+}  // namespace trb
+
+extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host, const void* b_host, void* c_host,
+                             float scale_a, float scale_b, int device_id, trb_result* out) {
+    clear_error();
+    if (out == nullptr || a_host == nullptr || b_host == nullptr || c_host == nullptr || m <= 0 || n <= 0 || k <= 0) {
+        set_error("trb_gemm_host: bad arguments");
+        return TRB_ERR_ARGS;
+    }
+    if (!gemm_dtype_supported(dtype)) {
+        set_error("unsupported dtype for native MFU kernel: %s", dtype_name(dtype));
+        return TRB_SKIPPED;
+    }
+    int rc = set_device(device_id);
+    if (rc != TRB_OK) return rc;
+    if (device_id >= 64) {
+        set_error("device id too large");
+        return TRB_ERR_ARGS;
+    }
+    fill_result_common(out, device_id);
+    GemmHostState& st = g_gemm_host[device_id];
+    std::lock_guard<std::mutex> lock(st.mu);
+    const size_t es = dtype_size(dtype);
+    const size_t ab = (size_t)m * k * es, bb = (size_t)k * n * es, cb = (size_t)m * n * gemm_out_size(dtype);
+    if ((rc = ensure(st, 0, ab)) != TRB_OK) return rc;
+    if ((rc = ensure(st, 1, bb)) != TRB_OK) return rc;
+    if ((rc = ensure(st, 2, cb)) != TRB_OK) return rc;
+    if (st.s == nullptr) {
+        TRB_CUDA(cudaStreamCreateWithFlags(&st.s, cudaStreamNonBlocking));
+        TRB_CUDA(cudaEventCreate(&st.start));
+        TRB_CUDA(cudaEventCreate(&st.stop));
+    }
+    TRB_CUDA(cudaEventRecord(st.start, st.s));
+    TRB_CUDA(cudaMemcpyAsync(st.buf[0], a_host, ab, cudaMemcpyHostToDevice, st.s));
+    TRB_CUDA(cudaMemcpyAsync(st.buf[1], b_host, bb, cudaMemcpyHostToDevice, st.s));
+    gemm::LaunchInfo info;
+    rc = gemm::launch(dtype, m, n, k, st.buf[0], st.buf[1], st.buf[2], scale_a, scale_b, st.s, &info);
+    if (rc != TRB_OK) return rc;
+    TRB_CUDA(cudaMemcpyAsync(c_host, st.buf[2], cb, cudaMemcpyDeviceToHost, st.s));
+    TRB_CUDA(cudaEventRecord(st.stop, st.s));
+    TRB_CUDA(cudaEventSynchronize(st.stop));
+    float ms = 0.f;
+    TRB_CUDA(cudaEventElapsedTime(&ms, st.start, st.stop));
+    out->elapsed_s = ms / 1000.0;
+    out->achieved_ops = 2.0 * (double)m * (double)n * (double)k;
+    out->h2d_bytes = (double)(ab + bb);
+    out->d2h_bytes = (double)cb;
+    out->grid = info.grid;
+    out->block = info.block;
+    out->launches = 1;
+    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_tma_ws_128x256+copies");
+    return check_device_errors(out);
+}

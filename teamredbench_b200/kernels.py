@@ -1,0 +1,83 @@
+"""torch-tensor front end of the native kernels.
+
+Thin: it checks shapes / dtypes / devices, takes raw device pointers and the
+current CUDA stream, and calls libtrb_b200 through ``_native``.  torch provides
+device memory and streams only; all arithmetic happens in the CUDA kernels.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+from teamredbench_b200 import _native
+
+_TORCH_TO_TRB = {
+    "torch.float32": "float32",
+    "torch.bfloat16": "bfloat16",
+    "torch.float16": "float16",
+    "torch.float64": "float64",
+    "torch.int8": "int8",
+    "torch.uint8": "int8",
+    "torch.float8_e4m3fn": "float8_e4m3fn",
+}
+
+
+def trb_dtype(tensor: Any) -> str:
+    name = _TORCH_TO_TRB.get(str(tensor.dtype))
+    if name is None:
+        raise _native.NativeSkipped(1, f"unsupported tensor dtype {tensor.dtype}")
+    return name
+
+
+def _stream_handle(tensor: Any, stream: Any | None) -> int:
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(tensor.device)
+    return int(stream.cuda_stream)
+
+
+def _require_cuda_contiguous(*tensors: Any) -> None:
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("tensor must live on a CUDA device")
+        if not t.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+
+
+def stream_op(mode: str, dst: Any, src: Any, aux: Any | None = None, scale: float = 1.0, variant: str = "auto",
+              blocks_per_sm: int = 0, stream: Any | None = None) -> Any:
+    """dst = copy / scale / triad of src (and aux) -- the hbm benchmark's op
+    (reference src/teamredbench/benchmarks/hbm.py:29-39), on the GPU."""
+    _require_cuda_contiguous(dst, src, aux)
+    if src.dtype != dst.dtype or (aux is not None and aux.dtype != src.dtype):
+        raise ValueError("dst, src and aux must share one dtype")
+    if src.numel() != dst.numel() or (aux is not None and aux.numel() != src.numel()):
+        raise ValueError("dst, src and aux must have the same number of elements")
+    if mode == "triad" and aux is None:
+        raise ValueError("triad needs aux")
+    _native.hbm_launch(trb_dtype(src), mode, dst.data_ptr(), src.data_ptr(),
+                       aux.data_ptr() if aux is not None else None, src.numel(), float(scale), variant,
+                       blocks_per_sm, _stream_handle(src, stream))
+    return dst
+
+
+def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float = 1.0, scale_b: float = 1.0,
+         stream: Any | None = None) -> Any:
+    """out = a @ b on the tcgen05 kernel; a (m x k) and b (k x n) row-major.
+
+    dtype defaults to the tensors' dtype; pass ``dtype="tfloat32"`` to run
+    float32 tensors on the tf32 tensor-core path.  Output dtypes: bf16 for
+    bf16 / e4m3 inputs, f16 for f16, f32 for tf32, int32 for int8."""
+    _require_cuda_contiguous(a, b, out)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"incompatible shapes {tuple(a.shape)} x {tuple(b.shape)}")
+    m, k = a.shape
+    n = b.shape[1]
+    if tuple(out.shape) != (m, n):
+        raise ValueError(f"out must be {(m, n)}, got {tuple(out.shape)}")
+    name = dtype or trb_dtype(a)
+    _native.gemm_launch(name, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), float(scale_a), float(scale_b),
+                        _stream_handle(a, stream))
+    return out

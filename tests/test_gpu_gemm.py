@@ -1,0 +1,138 @@
+"""GPU parity of the tcgen05 GEMM (through the C ABI) against the fp64 CPU
+oracle and the reference-generated torch golden vectors.
+
+Pass rule: max|C - ref| <= tol * max|ref| (the reference harness's metric,
+tests/native/gemm_parity.hip.cpp:163-178) with tol = 1e-2 for bf16 / f16 /
+e4m3 and 1e-5 for tf32; int8 must be bit-exact."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.helpers import GEMM_OUT, GEMM_TOLERANCE, from_raw, gemm_operands, gemm_result_f64, to_raw, torch_dtype
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover - CPU container
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from teamredbench_b200 import _native  # noqa: E402
+from teamredbench_b200.kernels import gemm  # noqa: E402
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DTYPES = ["bfloat16", "float16", "tfloat32", "float8_e4m3fn", "int8"]
+
+
+def _run(name, a, b, sa=1.0, sb=1.0):
+    m, n = a.shape[0], b.shape[1]
+    out = torch.empty((m, n), device="cuda", dtype=torch_dtype(GEMM_OUT[name]))
+    gemm(a, b, out, dtype=name, scale_a=sa, scale_b=sb)
+    torch.cuda.synchronize()
+    return out
+
+
+def _check(name, a, b, c, sa, sb, rows):
+    ref = oracle.gemm_rows(name, to_raw(a), to_raw(b), rows, sa, sb)
+    got = gemm_result_f64(name, c)[rows]
+    if name == "int8":
+        assert np.array_equal(got.astype(np.int64), ref.astype(np.int64))
+        return 0.0
+    err = oracle.rel_to_max_error(got, ref)
+    assert err <= GEMM_TOLERANCE[name], (name, err)
+    return err
+
+
+@pytest.mark.parametrize("key", ["square/bfloat16", "square/float16", "square/tfloat32", "square/float8_e4m3fn",
+                                 "square/int8", "ragged/bfloat16"])
+def test_golden_vectors(key):
+    g = np.load(GOLDEN / "gemm_golden.npz")
+    name = key.split("/")[1]
+    m, n, k = (int(v) for v in g[f"{key}/shape"])
+    a = from_raw(g[f"{key}/a"].reshape(m, k), name if name != "tfloat32" else "float32")
+    b = from_raw(g[f"{key}/b"].reshape(k, n), name if name != "tfloat32" else "float32")
+    sa, sb = (float(x) for x in g[f"{key}/scales"]) if name == "float8_e4m3fn" else (1.0, 1.0)
+    c = _run(name, a, b, sa, sb)
+    golden = g[f"{key}/c"].reshape(m, n)
+    got = gemm_result_f64(name, c)
+    if name == "int8":
+        assert np.array_equal(got.astype(np.int64), golden.astype(np.int64))
+    else:
+        want = (oracle.bf16_to_f32(golden) if GEMM_OUT[name] == "bfloat16" else golden).astype(np.float64)
+        assert oracle.rel_to_max_error(got, want) <= GEMM_TOLERANCE[name]
+    _check(name, a, b, c, sa, sb, np.arange(m))
+
+
+@pytest.mark.parametrize("name", DTYPES)
+@pytest.mark.parametrize("shape", [(128, 256, 128), (256, 512, 1024), (1024, 1024, 1024), (300, 528, 208),
+                                   (1, 16, 16), (129, 272, 144)])
+def test_shapes_full_compare(name, shape):
+    m, n, k = shape
+    if (n * (4 if name == "tfloat32" else 2 if name in ("bfloat16", "float16") else 1)) % 16:
+        pytest.skip("row stride not 16-byte aligned")
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=m + n + k)
+    c = _run(name, a, b, sa, sb)
+    _check(name, a, b, c, sa, sb, np.arange(m))
+
+
+@pytest.mark.parametrize("name", DTYPES)
+def test_baseline_8192_sampled_rows(name):
+    """BASELINE mixed-dtype sweep shape M=N=K=8192, 48 sampled rows vs fp64."""
+    m = n = k = 8192
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=0)
+    c = _run(name, a, b, sa, sb)
+    rows = np.random.default_rng(0).choice(m, size=48, replace=False)
+    _check(name, a, b, c, sa, sb, np.sort(rows))
+
+
+@pytest.mark.parametrize("m", [16, 128])
+def test_baseline_skinny_shapes(m):
+    a, b, sa, sb = gemm_operands("bfloat16", m, 8192, 8192, seed=1)
+    c = _run("bfloat16", a, b)
+    _check("bfloat16", a, b, c, 1.0, 1.0, np.arange(m))
+
+
+@pytest.mark.parametrize("size", [2048, 4096])
+def test_baseline_square_bf16_sweep_sampled(size):
+    a, b, _, _ = gemm_operands("bfloat16", size, size, size, seed=0)
+    c = _run("bfloat16", a, b)
+    rows = np.random.default_rng(size).choice(size, size=64, replace=False)
+    _check("bfloat16", a, b, c, 1.0, 1.0, np.sort(rows))
+
+
+def test_repeated_launches_are_deterministic():
+    a, b, _, _ = gemm_operands("bfloat16", 1024, 2048, 512, seed=3)
+    first = _run("bfloat16", a, b)
+    for _ in range(3):
+        assert torch.equal(_run("bfloat16", a, b), first)
+
+
+def test_host_entry_point():
+    m, n, k = 512, 768, 384
+    a, b, _, _ = gemm_operands("bfloat16", m, n, k, seed=5)
+    ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
+    hc = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+    res = _native.gemm_host("bfloat16", m, n, k, ha.data_ptr(), hb.data_ptr(), hc.data_ptr())
+    assert res.elapsed_s > 0 and res.device_error == 0
+    _check("bfloat16", a, b, hc, 1.0, 1.0, np.arange(m))
+
+
+def test_alignment_and_dtype_errors():
+    a = torch.zeros((64, 20), device="cuda", dtype=torch.bfloat16)  # 40-byte rows
+    b = torch.zeros((20, 64), device="cuda", dtype=torch.bfloat16)
+    out = torch.empty((64, 64), device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(_native.NativeError):
+        gemm(a, b, out)
+    x = torch.zeros((64, 64), device="cuda", dtype=torch.float64)
+    with pytest.raises(_native.NativeSkipped):
+        gemm(x, x, torch.empty_like(x))
+
+
+def test_run_entry_point_reports_timing():
+    res = _native.gemm_run("bfloat16", 2048, 2048, 2048, 1, 3)
+    assert res.elapsed_s > 0 and res.achieved_ops == 2 * 2048 ** 3 and res.device_error == 0
+    res = _native.gemm_run("float8_e4m3fn", 1024, 1024, 1024, 1, 2)
+    assert res.elapsed_s > 0 and res.device_error == 0
