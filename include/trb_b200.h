@@ -79,6 +79,8 @@ typedef struct trb_result {
     int32_t variant;         /* trb_hbm_variant actually used (hbm) */
     int32_t device_error;    /* non-zero if a bounded device wait gave up */
     int32_t launches;        /* kernels this library launched inside the timed loop */
+    int32_t split_k;         /* gemm: K splits used (1 = none) */
+    int32_t reserved;
     char implementation[64]; /* short name of the kernel that ran */
 } trb_result;
 
@@ -169,6 +171,18 @@ int trb_gemm_run(const trb_gemm_args* args, trb_result* out);
  * 229-234) and the native mfma_gemm_*_kernel launches. */
 int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
                     float scale_a, float scale_b, void* stream);
+
+/* trb_gemm_launch with an explicit split-K factor (0 = automatic, as
+ * trb_gemm_launch; >= 1 forces that many K splits, clamped to the number of
+ * 128-byte K blocks).  Splits > 1 use the library's per-device split-K
+ * workspace: fp32 partials plus per-tile counters, summed deterministically
+ * in split order by the last CTA of each tile.  Automatic mode splits only
+ * problems whose output tiles leave more than half of the SMs idle (e.g. the
+ * skinny M = 16 / 128 shapes).  No reference counterpart: the reference's
+ * native GEMM has no split-K (mfu_gemm_lowp.hip.hpp:423-431 launches one
+ * persistent grid over output tiles). */
+int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
+                       float scale_a, float scale_b, int splits, void* stream);
 
 /* Same GEMM over HOST arrays (copies in and out inside the call). */
 int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host, const void* b_host, void* c_host,

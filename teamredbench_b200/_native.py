@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "trb_hbm_host",
     "trb_gemm_run",
     "trb_gemm_launch",
+    "trb_gemm_launch_ex",
     "trb_gemm_host",
     "trb_round_tf32",
 )
@@ -77,6 +78,8 @@ class TrbResult(ctypes.Structure):
         ("variant", ctypes.c_int32),
         ("device_error", ctypes.c_int32),
         ("launches", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
         ("implementation", ctypes.c_char * 64),
     ]
 
@@ -145,6 +148,8 @@ def load() -> ctypes.CDLL:
     lib.trb_gemm_run.restype = i32
     lib.trb_gemm_launch.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, vp]
     lib.trb_gemm_launch.restype = i32
+    lib.trb_gemm_launch_ex.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, i32, vp]
+    lib.trb_gemm_launch_ex.restype = i32
     lib.trb_gemm_host.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, i32, res_p]
     lib.trb_gemm_host.restype = i32
     lib.trb_round_tf32.argtypes = [vp, u64, vp]
@@ -199,6 +204,11 @@ def gemm_run(dtype: str, m: int, n: int, k: int, warmup: int, iterations: int, d
 def gemm_launch(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,
                 scale_b: float = 1.0, stream: int = 0) -> None:
     check(load().trb_gemm_launch(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, stream or None))
+
+
+def gemm_launch_ex(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,
+                   scale_b: float = 1.0, splits: int = 0, stream: int = 0) -> None:
+    check(load().trb_gemm_launch_ex(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, splits, stream or None))
 
 
 def gemm_host(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,

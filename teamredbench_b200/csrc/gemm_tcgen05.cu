@@ -183,10 +183,24 @@ __device__ __forceinline__ void store_chunk(void* C, int row, int col, int N, co
     }
 }
 
+// Split-K parameters.  With splits == 1 each work unit is one output tile and
+// the epilogue stores C directly.  With splits > 1 a unit is (tile, split):
+// its k-block range is [split * kb_per_split, min(.. + kb_per_split, num_kb)),
+// the epilogue writes an fp32 partial to ws[unit] (kBM x kBN floats), and the
+// last unit of a tile to finish (per-tile arrival counter) sums the partials
+// of splits 0..S-1 in that fixed order -- deterministic -- then writes C and
+// resets the counter to 0 for the next launch.
+struct SplitK {
+    int splits;
+    int kb_per_split;
+    float* ws;
+    unsigned int* counters;
+};
+
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        void* __restrict__ C, int M, int N, int K, float out_scale) {
+                        void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
     using Tr = Traits<DT>;
     constexpr int kBKElems = kBKBytes / Tr::kEsize;         // K elements per stage
     constexpr int kBoxN = 128 / Tr::kEsize;                 // N elements per B box (one swizzle row)
@@ -202,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ __align__(8) uint64_t drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
+    __shared__ int last_split_flag;
 
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = smem_base;
@@ -213,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_n = (N + kBN - 1) / kBN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + kBKElems - 1) / kBKElems;
+    const int num_units = num_tiles * sk.splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -244,10 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;  // per stage: a load is outstanding / its parity
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+            for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
                 int mb, nb;
-                tile_coords(tile, num_m, num_n, mb, nb);
-                for (int kb = 0; kb < num_kb; ++kb) {
+                tile_coords(unit / sk.splits, num_m, num_n, mb, nb);
+                const int kb0 = (unit % sk.splits) * sk.kb_per_split;
+                const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrProducerWait);
                         abort_flag = 1;
@@ -281,7 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, phase = 0;
             bool ok = true;
             int t_local = 0;
-            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++t_local) {
+            for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++t_local) {
+                const int kb0 = (unit % sk.splits) * sk.kb_per_split;
+                const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
                 const int acc = t_local & 1;
                 const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
                 if (!mbar_wait(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
@@ -291,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
@@ -306,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t a_desc = make_sdesc(a_base + ks * kInstrKBytes, 16, 1024);
                         const uint64_t b_desc = make_sdesc(b_base + ks * kInstrKRows * 128, kBBoxBytes,
                                                            Tr::BLayout::kSbo, Tr::BLayout::kLayoutType);
-                        mma<Tr::kKind>(d_tmem, a_desc, b_desc, Tr::kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                        mma<Tr::kKind>(d_tmem, a_desc, b_desc, Tr::kIdesc, (kb != kb0 || ks != 0) ? 1u : 0u);
                     }
                     tc_commit(smem_u32(&empty_bar[stage]));  // frees the smem stage when these MMAs finish
                     if (++stage == kStages) {
@@ -324,14 +344,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
         const int q = warp & 3;
         const int row_in_tile = q * 32 + lane;
+        const bool first_epi_thread = threadIdx.x == 64;
         int t_local = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t_local) {
+        for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++t_local) {
+            const int tile = unit / sk.splits;
             int mb, nb;
             tile_coords(tile, num_m, num_n, mb, nb);
             const int acc = t_local & 1;
             const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
             bool ok = mbar_wait(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
             ok = __all_sync(0xffffffffu, ok);
+            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);  // the fix-up below is CTA-wide
             if (!ok) {
                 if (lane == 0) {
                     atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
@@ -342,17 +365,79 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int grow = mb * kBM + row_in_tile;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+            if (sk.splits == 1) {
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+                    tmem_wait_ld();
+                    const int gcol = nb * kBN + c * 32;
+                    if (grow < M && gcol < N) store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
+                continue;
+            }
+            // ---- split-K: publish this unit's fp32 partial
+            float* wrow = sk.ws + ((size_t)unit * kBM + row_in_tile) * kBN;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
                 tmem_wait_ld();
-                const int gcol = nb * kBN + c * 32;
-                if (grow < M && gcol < N) store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+                if (grow < M && nb * kBN + c * 32 < N) {
+                    uint4* w4 = reinterpret_cast<uint4*>(wrow + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) w4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+                }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
+            if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));  // TMEM free for the next unit
+            __threadfence();
+            named_barrier(1, 128);
+            if (first_epi_thread)
+                last_split_flag = atomicAdd(&sk.counters[tile], 1u) == (unsigned)(sk.splits - 1);
+            named_barrier(1, 128);
+            if (!last_split_flag) continue;
+            // ---- last arrival: deterministic sum over splits 0..S-1, convert, store C
+            __threadfence();
+            if (grow < M) {
+                const float* base = sk.ws + ((size_t)tile * sk.splits * kBM + row_in_tile) * kBN;
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    const int gcol = nb * kBN + c * 32;
+                    if (gcol >= N) break;
+                    float acc_f[32];
+                    const float4* p0 = reinterpret_cast<const float4*>(base + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 v = __ldcg(p0 + i);
+                        acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
+                    }
+                    for (int sp = 1; sp < sk.splits; ++sp) {
+                        const float4* ps = reinterpret_cast<const float4*>(base + (size_t)sp * kBM * kBN + c * 32);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 v = __ldcg(ps + i);
+                            if constexpr (DT == TRB_INT8) {  // exact integer partial sums
+                                acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
+                                acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
+                                acc_f[4 * i + 2] = __int_as_float(__float_as_int(acc_f[4 * i + 2]) + __float_as_int(v.z));
+                                acc_f[4 * i + 3] = __int_as_float(__float_as_int(acc_f[4 * i + 3]) + __float_as_int(v.w));
+                            } else {
+                                acc_f[4 * i] += v.x; acc_f[4 * i + 1] += v.y; acc_f[4 * i + 2] += v.z; acc_f[4 * i + 3] += v.w;
+                            }
+                        }
+                    }
+                    uint32_t r[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(acc_f[i]);
+                    store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+                }
+            }
+            if (first_epi_thread) sk.counters[tile] = 0u;  // ready for the next launch
         }
     }
 
@@ -402,8 +487,56 @@ static int encode_2d(CUtensorMap* map, const void* base, int esize, uint64_t inn
     return TRB_OK;
 }
 
+// Split-K workspace of one device: fp32 partials + per-tile arrival counters.
+// Grow-only, allocated on first use; counters are zeroed when allocated and
+// every launch leaves them at zero.  Launches that overlap on one device
+// would share it, hence the one-call-per-device rule of the C ABI.
+struct Workspace {
+    float* ws = nullptr;
+    size_t ws_bytes = 0;
+    unsigned int* counters = nullptr;
+    size_t counter_count = 0;
+    std::mutex mu;
+};
+static Workspace g_workspace[64];
+
+static int ensure_workspace(int dev, size_t ws_bytes, size_t counters, SplitK* sk) {
+    if (dev < 0 || dev >= 64) {
+        set_error("device id %d out of range for the split-K workspace", dev);
+        return TRB_ERR_ARGS;
+    }
+    Workspace& w = g_workspace[dev];
+    std::lock_guard<std::mutex> lock(w.mu);
+    if (w.ws_bytes < ws_bytes) {
+        if (w.ws) cudaFree(w.ws);
+        w.ws = nullptr;
+        w.ws_bytes = 0;
+        TRB_CUDA(cudaMalloc(&w.ws, ws_bytes));
+        w.ws_bytes = ws_bytes;
+    }
+    if (w.counter_count < counters) {
+        if (w.counters) cudaFree(w.counters);
+        w.counters = nullptr;
+        w.counter_count = 0;
+        TRB_CUDA(cudaMalloc(&w.counters, counters * sizeof(unsigned int)));
+        TRB_CUDA(cudaMemset(w.counters, 0, counters * sizeof(unsigned int)));
+        w.counter_count = counters;
+    }
+    sk->ws = w.ws;
+    sk->counters = w.counters;
+    return TRB_OK;
+}
+
+// Splits for a problem: split K only when the output tiles leave more than
+// half of the SMs idle (skinny M or small N), keeping >= 4 k-blocks per split.
+static int choose_splits(long tiles, int num_kb, int sms) {
+    if (tiles * 2 > sms) return 1;
+    long s = std::min<long>(sms / std::max<long>(tiles, 1), num_kb / 4);
+    return (int)std::max<long>(1, std::min<long>(s, 16));
+}
+
 template <int DT>
-static int launch_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale,
+static int launch_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale, int splits,
                         cudaStream_t stream, LaunchInfo* info) {
     using Tr = Traits<DT>;
     constexpr int es = Tr::kEsize;
@@ -422,15 +555,26 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     }
     const int sms = device_sm_count(dev);
     const long tiles = (long)((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
-    const int grid = (int)std::max<long>(1, std::min<long>(tiles, sms));
-    gemm_tcgen05_kernel<DT><<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, c, m, n, k, out_scale);
+    const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
+    if (splits <= 0) splits = choose_splits(tiles, num_kb, sms);
+    splits = std::max(1, std::min(splits, num_kb));
+    const int kbps = (num_kb + splits - 1) / splits;
+    splits = (num_kb + kbps - 1) / kbps;  // every split owns at least one k-block
+    SplitK sk{splits, kbps, nullptr, nullptr};
+    if (splits > 1) {
+        rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * kBN * sizeof(float), (size_t)tiles, &sk);
+        if (rc != TRB_OK) return rc;
+    }
+    const long units = tiles * splits;
+    const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
+    gemm_tcgen05_kernel<DT><<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, c, m, n, k, out_scale, sk);
     TRB_CUDA(cudaGetLastError());
-    if (info) *info = {grid, kThreads};
+    if (info) *info = {grid, kThreads, splits};
     return TRB_OK;
 }
 
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
-           cudaStream_t stream, LaunchInfo* info) {
+           int splits, cudaStream_t stream, LaunchInfo* info) {
     if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || b == nullptr || c == nullptr) {
         set_error("trb_gemm_launch: dimensions must be positive and pointers non-null");
         return TRB_ERR_ARGS;
@@ -450,13 +594,17 @@ int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c
         set_error("trb_gemm_launch: A, B and C must be 16-byte aligned");
         return TRB_ERR_ALIGN;
     }
+    if (splits < 0) {
+        set_error("trb_gemm_launch: splits must be >= 0");
+        return TRB_ERR_ARGS;
+    }
     switch (dtype) {
-        case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16>(m, n, k, a, b, c, 1.0f, stream, info);
-        case TRB_FLOAT16: return launch_typed<TRB_FLOAT16>(m, n, k, a, b, c, 1.0f, stream, info);
-        case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32>(m, n, k, a, b, c, 1.0f, stream, info);
+        case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16>(m, n, k, a, b, c, 1.0f, splits, stream, info);
+        case TRB_FLOAT16: return launch_typed<TRB_FLOAT16>(m, n, k, a, b, c, 1.0f, splits, stream, info);
+        case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32>(m, n, k, a, b, c, 1.0f, splits, stream, info);
         case TRB_FLOAT8_E4M3FN:
-            return launch_typed<TRB_FLOAT8_E4M3FN>(m, n, k, a, b, c, scale_a * scale_b, stream, info);
-        default: return launch_typed<TRB_INT8>(m, n, k, a, b, c, 1.0f, stream, info);
+            return launch_typed<TRB_FLOAT8_E4M3FN>(m, n, k, a, b, c, scale_a * scale_b, splits, stream, info);
+        default: return launch_typed<TRB_INT8>(m, n, k, a, b, c, 1.0f, splits, stream, info);
     }
 }
 
@@ -568,7 +716,14 @@ int read_error(bool clear) {
 extern "C" int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a,
                                float scale_b, void* stream) {
     trb::clear_error();
-    return trb::gemm::launch(dtype, m, n, k, a, b, c, scale_a, scale_b, static_cast<cudaStream_t>(stream), nullptr);
+    return trb::gemm::launch(dtype, m, n, k, a, b, c, scale_a, scale_b, 0, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a,
+                                  float scale_b, int splits, void* stream) {
+    trb::clear_error();
+    return trb::gemm::launch(dtype, m, n, k, a, b, c, scale_a, scale_b, splits, static_cast<cudaStream_t>(stream),
+                             nullptr);
 }
 
 extern "C" int trb_round_tf32(void* data, uint64_t count, void* stream) {

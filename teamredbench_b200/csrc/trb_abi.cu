@@ -374,13 +374,13 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
 
     gemm::LaunchInfo info;
     for (int i = 0; i < args->warmup; ++i) {
-        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, se.stream, &info);
+        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, 0, se.stream, &info);
         if (rc != TRB_OK) return rc;
     }
     TRB_CUDA(cudaStreamSynchronize(se.stream));
     TRB_CUDA(cudaEventRecord(se.start, se.stream));
     for (int i = 0; i < args->iterations; ++i) {
-        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, se.stream, &info);
+        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, 0, se.stream, &info);
         if (rc != TRB_OK) return rc;
     }
     TRB_CUDA(cudaEventRecord(se.stop, se.stream));
@@ -392,8 +392,10 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
     out->grid = info.grid;
     out->block = info.block;
     out->blocks_per_sm = 1;
+    out->split_k = info.splits;
     out->launches = args->iterations;
-    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_tma_ws_128x256");
+    snprintf(out->implementation, sizeof(out->implementation), info.splits > 1 ? "tcgen05_tma_ws_128x256_splitk"
+                                                                                : "tcgen05_tma_ws_128x256");
     return check_device_errors(out);
 }
 
@@ -452,7 +454,7 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     TRB_CUDA(cudaMemcpyAsync(st.buf[0], a_host, ab, cudaMemcpyHostToDevice, st.s));
     TRB_CUDA(cudaMemcpyAsync(st.buf[1], b_host, bb, cudaMemcpyHostToDevice, st.s));
     gemm::LaunchInfo info;
-    rc = gemm::launch(dtype, m, n, k, st.buf[0], st.buf[1], st.buf[2], scale_a, scale_b, st.s, &info);
+    rc = gemm::launch(dtype, m, n, k, st.buf[0], st.buf[1], st.buf[2], scale_a, scale_b, 0, st.s, &info);
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaMemcpyAsync(c_host, st.buf[2], cb, cudaMemcpyDeviceToHost, st.s));
     TRB_CUDA(cudaEventRecord(st.stop, st.s));
@@ -463,6 +465,7 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     out->achieved_ops = 2.0 * (double)m * (double)n * (double)k;
     out->h2d_bytes = (double)(ab + bb);
     out->d2h_bytes = (double)cb;
+    out->split_k = info.splits;
     out->grid = info.grid;
     out->block = info.block;
     out->launches = 1;

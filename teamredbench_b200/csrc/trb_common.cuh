@@ -46,10 +46,11 @@ int read_error(bool clear);
 
 namespace gemm {
 struct LaunchInfo {
-    int grid = 0, block = 0;
+    int grid = 0, block = 0, splits = 1;
 };
+// splits: 0 = automatic (split-K only for problems that leave SMs idle), >= 1 forced.
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
-           cudaStream_t stream, LaunchInfo* info);
+           int splits, cudaStream_t stream, LaunchInfo* info);
 int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsigned int* absmax_scratch,
                  float* scale_out, cudaStream_t stream);
 int read_error(bool clear);

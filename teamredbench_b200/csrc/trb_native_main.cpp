@@ -151,7 +151,7 @@ int main(int argc, char** argv) {
     std::printf("{\"status\":\"ok\",\"raw_metrics\":{\"elapsed_s\":%.9e,\"achieved_ops\":%.0f},\"metadata\":{",
                 r.elapsed_s, r.achieved_ops);
     print_common_metadata(r);
-    std::printf(",\"tile_m\":128,\"tile_n\":256,\"k_stage_bytes\":128,\"stages\":4}}\n");
+    std::printf(",\"tile_m\":128,\"tile_n\":256,\"k_stage_bytes\":128,\"stages\":4,\"split_k\":%d}}\n", r.split_k);
 #endif
     std::fflush(stdout);
     return 0;

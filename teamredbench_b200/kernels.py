@@ -64,12 +64,13 @@ def stream_op(mode: str, dst: Any, src: Any, aux: Any | None = None, scale: floa
 
 
 def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float = 1.0, scale_b: float = 1.0,
-         stream: Any | None = None) -> Any:
+         splits: int = 0, stream: Any | None = None) -> Any:
     """out = a @ b on the tcgen05 kernel; a (m x k) and b (k x n) row-major.
 
     dtype defaults to the tensors' dtype; pass ``dtype="tfloat32"`` to run
     float32 tensors on the tf32 tensor-core path.  Output dtypes: bf16 for
-    bf16 / e4m3 inputs, f16 for f16, f32 for tf32, int32 for int8."""
+    bf16 / e4m3 inputs, f16 for f16, f32 for tf32, int32 for int8.
+    splits: 0 = automatic split-K, >= 1 forces that many K splits."""
     _require_cuda_contiguous(a, b, out)
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
         raise ValueError(f"incompatible shapes {tuple(a.shape)} x {tuple(b.shape)}")
@@ -78,6 +79,6 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     if tuple(out.shape) != (m, n):
         raise ValueError(f"out must be {(m, n)}, got {tuple(out.shape)}")
     name = dtype or trb_dtype(a)
-    _native.gemm_launch(name, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), float(scale_a), float(scale_b),
-                        _stream_handle(a, stream))
+    _native.gemm_launch_ex(name, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), float(scale_a),
+                           float(scale_b), int(splits), _stream_handle(a, stream))
     return out
