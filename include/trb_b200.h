@@ -102,14 +102,28 @@ typedef struct trb_hbm_args {
 
 /* Arguments of one mfu case; mirrors --dtype --m --n --k --warmup --iterations
  * --device-id (src/teamredbench/benchmarks/mfu.py:107-125). */
+/* Storage of the B operand of a GEMM. */
+typedef enum trb_b_layout {
+    TRB_B_ROW_MAJOR = 0,  /* B is the row-major K x N matrix (an MN-major tensor-core operand) */
+    TRB_B_K_MAJOR = 1     /* B is stored transposed: row-major N x K (a K-major operand) */
+} trb_b_layout;
+
 typedef struct trb_gemm_args {
     int32_t dtype;           /* BFLOAT16, FLOAT16, TFLOAT32, FLOAT8_E4M3FN or INT8 */
     int32_t m, n, k;
     int32_t warmup;
     int32_t iterations;
     int32_t device_id;
-    int32_t reserved;
+    int32_t b_layout;        /* trb_b_layout of the generated B (the reference packs B K-contiguous, untimed) */
 } trb_gemm_args;
+
+/* Kernel choices for trb_gemm_launch_ex. */
+typedef struct trb_gemm_options {
+    int32_t splits;          /* 0 = automatic split-K; >= 1 forces that many K splits */
+    int32_t cta_pair;        /* < 0 automatic, 0 = single-CTA 128 x 256 tiles, > 0 = CTA-pair 256 x 256 tiles */
+    int32_t b_layout;        /* trb_b_layout */
+    int32_t reserved;
+} trb_gemm_options;
 
 /* ---- library ------------------------------------------------------------ */
 
@@ -172,17 +186,22 @@ int trb_gemm_run(const trb_gemm_args* args, trb_result* out);
 int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
                     float scale_a, float scale_b, void* stream);
 
-/* trb_gemm_launch with an explicit split-K factor (0 = automatic, as
- * trb_gemm_launch; >= 1 forces that many K splits, clamped to the number of
- * 128-byte K blocks).  Splits > 1 use the library's per-device split-K
- * workspace: fp32 partials plus per-tile counters, summed deterministically
- * in split order by the last CTA of each tile.  Automatic mode splits only
- * problems whose output tiles leave more than half of the SMs idle (e.g. the
- * skinny M = 16 / 128 shapes).  No reference counterpart: the reference's
- * native GEMM has no split-K (mfu_gemm_lowp.hip.hpp:423-431 launches one
- * persistent grid over output tiles). */
+/* trb_gemm_launch with explicit kernel choices (options may be NULL: all automatic).
+ *  splits:   >= 1 forces that many K splits (clamped to the number of 128-byte
+ *            K blocks).  Splits > 1 use the library's per-device split-K
+ *            workspace (fp32 partials and per-tile counters; the last CTA of a
+ *            tile sums the partials in split order, so results are
+ *            deterministic).  Automatic mode splits only problems whose output
+ *            tiles leave more than half of the tile workers idle (e.g. the
+ *            skinny M = 16 / 128 shapes).
+ *  cta_pair: the CTA-pair kernel (tcgen05.mma.cta_group::2, 256 x 256 tiles)
+ *            or the single-CTA kernel (128 x 256 tiles); automatic = the pair
+ *            for 8-bit inputs, one CTA for 16/32-bit inputs.
+ *  b_layout: TRB_B_K_MAJOR reads b as B^T (row-major N x K).
+ * No reference counterpart: the reference's native GEMM has one tile shape
+ * and no split-K (mfu_gemm_lowp.hip.hpp:423-431). */
 int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
-                       float scale_a, float scale_b, int splits, void* stream);
+                       float scale_a, float scale_b, const trb_gemm_options* options, void* stream);
 
 /* Same GEMM over HOST arrays (copies in and out inside the call). */
 int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host, const void* b_host, void* c_host,

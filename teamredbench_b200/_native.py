@@ -113,8 +113,20 @@ class GemmArgs(ctypes.Structure):
         ("warmup", ctypes.c_int32),
         ("iterations", ctypes.c_int32),
         ("device_id", ctypes.c_int32),
+        ("b_layout", ctypes.c_int32),
+    ]
+
+
+class GemmOptions(ctypes.Structure):
+    _fields_ = [
+        ("splits", ctypes.c_int32),
+        ("cta_pair", ctypes.c_int32),
+        ("b_layout", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
     ]
+
+
+B_LAYOUTS = {"row_major": 0, "k_major": 1}
 
 
 _lib: ctypes.CDLL | None = None
@@ -148,7 +160,7 @@ def load() -> ctypes.CDLL:
     lib.trb_gemm_run.restype = i32
     lib.trb_gemm_launch.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, vp]
     lib.trb_gemm_launch.restype = i32
-    lib.trb_gemm_launch_ex.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, i32, vp]
+    lib.trb_gemm_launch_ex.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, ctypes.POINTER(GemmOptions), vp]
     lib.trb_gemm_launch_ex.restype = i32
     lib.trb_gemm_host.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, i32, res_p]
     lib.trb_gemm_host.restype = i32
@@ -194,8 +206,9 @@ def hbm_host(dtype: str, mode: str, dst: int, src: int, aux: int | None, count: 
     return result
 
 
-def gemm_run(dtype: str, m: int, n: int, k: int, warmup: int, iterations: int, device_id: int = 0) -> TrbResult:
-    args = GemmArgs(DTYPE_CODES[dtype], m, n, k, warmup, iterations, device_id, 0)
+def gemm_run(dtype: str, m: int, n: int, k: int, warmup: int, iterations: int, device_id: int = 0,
+             b_layout: str = "row_major") -> TrbResult:
+    args = GemmArgs(DTYPE_CODES[dtype], m, n, k, warmup, iterations, device_id, B_LAYOUTS[b_layout])
     result = TrbResult()
     check(load().trb_gemm_run(ctypes.byref(args), ctypes.byref(result)))
     return result
@@ -207,8 +220,11 @@ def gemm_launch(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scal
 
 
 def gemm_launch_ex(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,
-                   scale_b: float = 1.0, splits: int = 0, stream: int = 0) -> None:
-    check(load().trb_gemm_launch_ex(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, splits, stream or None))
+                   scale_b: float = 1.0, splits: int = 0, cta_pair: int = -1, b_layout: str = "row_major",
+                   stream: int = 0) -> None:
+    opts = GemmOptions(splits, cta_pair, B_LAYOUTS[b_layout], 0)
+    check(load().trb_gemm_launch_ex(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, ctypes.byref(opts),
+                                    stream or None))
 
 
 def gemm_host(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,

@@ -352,6 +352,10 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
         set_error("unsupported dtype for native MFU kernel: %s", dtype_name(args->dtype));
         return TRB_SKIPPED;
     }
+    if (args->b_layout != TRB_B_ROW_MAJOR && args->b_layout != TRB_B_K_MAJOR) {
+        set_error("unknown b_layout %d", args->b_layout);
+        return TRB_ERR_ARGS;
+    }
     int rc = set_device(args->device_id);
     if (rc != TRB_OK) return rc;
     fill_result_common(out, args->device_id);
@@ -374,13 +378,15 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
 
     gemm::LaunchInfo info;
     for (int i = 0; i < args->warmup; ++i) {
-        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, 0, se.stream, &info);
+        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, 0, -1,
+                          args->b_layout == TRB_B_K_MAJOR, se.stream, &info);
         if (rc != TRB_OK) return rc;
     }
     TRB_CUDA(cudaStreamSynchronize(se.stream));
     TRB_CUDA(cudaEventRecord(se.start, se.stream));
     for (int i = 0; i < args->iterations; ++i) {
-        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, 0, se.stream, &info);
+        rc = gemm::launch(args->dtype, args->m, args->n, args->k, a, b, c, sa, sb, 0, -1,
+                          args->b_layout == TRB_B_K_MAJOR, se.stream, &info);
         if (rc != TRB_OK) return rc;
     }
     TRB_CUDA(cudaEventRecord(se.stop, se.stream));
@@ -394,8 +400,8 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
     out->blocks_per_sm = 1;
     out->split_k = info.splits;
     out->launches = args->iterations;
-    snprintf(out->implementation, sizeof(out->implementation), info.splits > 1 ? "tcgen05_tma_ws_128x256_splitk"
-                                                                                : "tcgen05_tma_ws_128x256");
+    snprintf(out->implementation, sizeof(out->implementation), "%s%s",
+             info.pair ? "tcgen05_cta_pair_256x256" : "tcgen05_1cta_128x256", info.splits > 1 ? "_splitk" : "");
     return check_device_errors(out);
 }
 
@@ -454,7 +460,7 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     TRB_CUDA(cudaMemcpyAsync(st.buf[0], a_host, ab, cudaMemcpyHostToDevice, st.s));
     TRB_CUDA(cudaMemcpyAsync(st.buf[1], b_host, bb, cudaMemcpyHostToDevice, st.s));
     gemm::LaunchInfo info;
-    rc = gemm::launch(dtype, m, n, k, st.buf[0], st.buf[1], st.buf[2], scale_a, scale_b, 0, st.s, &info);
+    rc = gemm::launch(dtype, m, n, k, st.buf[0], st.buf[1], st.buf[2], scale_a, scale_b, 0, -1, 0, st.s, &info);
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaMemcpyAsync(c_host, st.buf[2], cb, cudaMemcpyDeviceToHost, st.s));
     TRB_CUDA(cudaEventRecord(st.stop, st.s));
@@ -469,6 +475,7 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     out->grid = info.grid;
     out->block = info.block;
     out->launches = 1;
-    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_tma_ws_128x256+copies");
+    snprintf(out->implementation, sizeof(out->implementation), "%s+copies",
+             info.pair ? "tcgen05_cta_pair_256x256" : "tcgen05_1cta_128x256");
     return check_device_errors(out);
 }

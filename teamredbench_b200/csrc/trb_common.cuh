@@ -46,11 +46,13 @@ int read_error(bool clear);
 
 namespace gemm {
 struct LaunchInfo {
-    int grid = 0, block = 0, splits = 1;
+    int grid = 0, block = 0, splits = 1, pair = 0;
 };
 // splits: 0 = automatic (split-K only for problems that leave SMs idle), >= 1 forced.
+// cta_pair: < 0 automatic (pair for 8-bit inputs, single CTA otherwise), 0 single-CTA, > 0 CTA pair.
+// b_kmajor: B is stored N x K (K-major) instead of the row-major K x N matrix.
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
-           int splits, cudaStream_t stream, LaunchInfo* info);
+           int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info);
 int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsigned int* absmax_scratch,
                  float* scale_out, cudaStream_t stream);
 int read_error(bool clear);
@@ -221,6 +223,94 @@ TRB_DEFINE_MMA(mma_tf32, "tf32")
 TRB_DEFINE_MMA(mma_f8f6f4, "f8f6f4")
 TRB_DEFINE_MMA(mma_i8, "i8")
 #undef TRB_DEFINE_MMA
+
+// ---- CTA pairs (clusters of 2) and tcgen05 cta_group::2 ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (barriers that the peer CTA signals).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const volatile int* abort) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (abort != nullptr && *abort) return false;
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+        }
+    }
+}
+// The pair's even CTA (rank 0) owns the barriers that both CTAs' TMA loads
+// complete on; clearing bit 24 of a shared::cluster address selects it.
+constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;
+
+// 2-D tiled TMA load whose completion is signalled on a barrier of either CTA
+// of the pair (no multicast: each CTA loads only its own operand halves).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrive on `bar` (same offset) in every CTA of `mask` when this thread's
+// prior cta_group::2 tcgen05 ops complete.
+__device__ __forceinline__ void tc_commit_pair_multicast(uint32_t bar, uint16_t mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                     "r"(bar),
+                 "h"(mask)
+                 : "memory");
+}
+#define TRB_DEFINE_MMA_PAIR(NAME, KIND)                                                                    \
+    __device__ __forceinline__ void NAME(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, \
+                                         uint32_t accumulate) {                                           \
+        asm volatile(                                                                                      \
+            "{\n\t.reg .pred p;\n\t"                                                                       \
+            "setp.ne.b32 p, %4, 0;\n\t"                                                                    \
+            "tcgen05.mma.cta_group::2.kind::" KIND " [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),             \
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)                                          \
+            : "memory");                                                                                   \
+    }
+TRB_DEFINE_MMA_PAIR(mma_pair_f16, "f16")
+TRB_DEFINE_MMA_PAIR(mma_pair_tf32, "tf32")
+TRB_DEFINE_MMA_PAIR(mma_pair_f8f6f4, "f8f6f4")
+TRB_DEFINE_MMA_PAIR(mma_pair_i8, "i8")
+#undef TRB_DEFINE_MMA_PAIR
 
 // 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -5,6 +5,8 @@
 //   trb_hbm --dtype D --mode M --size-mib S --warmup W --iterations I --device-id G --scale X
 //           [--blocks-per-cu B] [--variant auto|vec|bulk|memcpy]
 //   trb_mfu --dtype D --m M --n N --k K --warmup W --iterations I --device-id G [--blocks-per-cu B]
+//           [--b-layout k_major|row_major]   (B generated K-contiguous by default: the reference's
+//           native GEMM likewise packs B K-contiguous outside the timed loop, mfu_gemm_lowp.hip.hpp:396-409)
 // The last stdout line is one JSON object: {"status":"ok","raw_metrics":{...},"metadata":{...}},
 // or {"status":"skipped","error":"..."} with exit status 0 for unsupported
 // input and failures, as the reference executables do
@@ -71,6 +73,7 @@ int main(int argc, char** argv) {
     double scale = 1.0;
 #else
     long long m = 4096, n = 4096, k = 4096;
+    std::string b_layout = "k_major";
 #endif
     for (int i = 1; i < argc; ++i) {
         const std::string key = argv[i];
@@ -95,6 +98,7 @@ int main(int argc, char** argv) {
         else if (key == "--m") ok = parse_int(value, &m);
         else if (key == "--n") ok = parse_int(value, &n);
         else if (key == "--k") ok = parse_int(value, &k);
+        else if (key == "--b-layout") b_layout = value;
 #endif
         else return emit_skipped(("unknown argument " + key).c_str());
         if (!ok) return emit_skipped(("invalid value for argument " + key).c_str());
@@ -146,12 +150,14 @@ int main(int argc, char** argv) {
     a.warmup = (int)warmup;
     a.iterations = (int)iterations;
     a.device_id = (int)device_id;
+    if (b_layout != "k_major" && b_layout != "row_major") return emit_skipped(("unknown --b-layout " + b_layout).c_str());
+    a.b_layout = b_layout == "k_major" ? TRB_B_K_MAJOR : TRB_B_ROW_MAJOR;
     const int rc = trb_gemm_run(&a, &r);
     if (rc != TRB_OK) return emit_skipped(trb_last_error());
     std::printf("{\"status\":\"ok\",\"raw_metrics\":{\"elapsed_s\":%.9e,\"achieved_ops\":%.0f},\"metadata\":{",
                 r.elapsed_s, r.achieved_ops);
     print_common_metadata(r);
-    std::printf(",\"tile_m\":128,\"tile_n\":256,\"k_stage_bytes\":128,\"stages\":4,\"split_k\":%d}}\n", r.split_k);
+    std::printf(",\"k_stage_bytes\":128,\"split_k\":%d,\"b_layout\":\"%s\"}}\n", r.split_k, b_layout.c_str());
 #endif
     std::fflush(stdout);
     return 0;

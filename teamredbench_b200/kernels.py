@@ -64,21 +64,25 @@ def stream_op(mode: str, dst: Any, src: Any, aux: Any | None = None, scale: floa
 
 
 def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float = 1.0, scale_b: float = 1.0,
-         splits: int = 0, stream: Any | None = None) -> Any:
+         splits: int = 0, cta_pair: int = -1, b_transposed: bool = False, stream: Any | None = None) -> Any:
     """out = a @ b on the tcgen05 kernel; a (m x k) and b (k x n) row-major.
+    With b_transposed=True, `b` holds B^T as a row-major (n x k) tensor.
 
     dtype defaults to the tensors' dtype; pass ``dtype="tfloat32"`` to run
     float32 tensors on the tf32 tensor-core path.  Output dtypes: bf16 for
     bf16 / e4m3 inputs, f16 for f16, f32 for tf32, int32 for int8.
-    splits: 0 = automatic split-K, >= 1 forces that many K splits."""
+    splits: 0 = automatic split-K, >= 1 forces that many K splits.
+    cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel."""
     _require_cuda_contiguous(a, b, out)
-    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
-        raise ValueError(f"incompatible shapes {tuple(a.shape)} x {tuple(b.shape)}")
+    bk, bn = (b.shape[1], b.shape[0]) if b_transposed else (b.shape[0], b.shape[1])
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != bk:
+        raise ValueError(f"incompatible shapes {tuple(a.shape)} x {tuple(b.shape)} (b_transposed={b_transposed})")
     m, k = a.shape
-    n = b.shape[1]
+    n = bn
     if tuple(out.shape) != (m, n):
         raise ValueError(f"out must be {(m, n)}, got {tuple(out.shape)}")
     name = dtype or trb_dtype(a)
     _native.gemm_launch_ex(name, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), float(scale_a),
-                           float(scale_b), int(splits), _stream_handle(a, stream))
+                           float(scale_b), int(splits), int(cta_pair), "k_major" if b_transposed else "row_major",
+                           _stream_handle(a, stream))
     return out

@@ -27,10 +27,10 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 DTYPES = ["bfloat16", "float16", "tfloat32", "float8_e4m3fn", "int8"]
 
 
-def _run(name, a, b, sa=1.0, sb=1.0, splits=0):
+def _run(name, a, b, sa=1.0, sb=1.0, splits=0, cta_pair=-1):
     m, n = a.shape[0], b.shape[1]
     out = torch.empty((m, n), device="cuda", dtype=torch_dtype(GEMM_OUT[name]))
-    gemm(a, b, out, dtype=name, scale_a=sa, scale_b=sb, splits=splits)
+    gemm(a, b, out, dtype=name, scale_a=sa, scale_b=sb, splits=splits, cta_pair=cta_pair)
     torch.cuda.synchronize()
     return out
 
@@ -124,10 +124,32 @@ def test_split_k_fixup(name, shape, splits):
     _check(name, a, b, c1, sa, sb, rows, tol=GEMM_TOLERANCE.get(name, 0) * (1.5 if name == "tfloat32" else 1))
 
 
+@pytest.mark.parametrize("name", DTYPES)
+@pytest.mark.parametrize("cta_pair", [0, 1])
+@pytest.mark.parametrize("shape,splits", [((300, 528, 208), 1), ((520, 784, 1024), 1), ((1, 16, 16), 1),
+                                          ((257, 272, 512), 3), ((384, 1024, 2048), 0)])
+def test_single_cta_and_pair_kernels(name, cta_pair, shape, splits):
+    """Both kernel shapes (1 CTA 128x256 / CTA pair 256x256), ragged M / N / K
+    tails, with and without split-K, against the oracle."""
+    m, n, k = shape
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=m * 7 + n)
+    c = _run(name, a, b, sa, sb, splits=splits, cta_pair=cta_pair)
+    _check(name, a, b, c, sa, sb, np.arange(m))
+
+
+def test_pair_and_single_agree_bitwise_for_int8():
+    a, b, _, _ = gemm_operands("int8", 1000, 1040, 3008, seed=9)
+    assert torch.equal(_run("int8", a, b, cta_pair=0), _run("int8", a, b, cta_pair=1))
+
+
 def test_split_k_run_entry_reports_splits():
     res = _native.gemm_run("bfloat16", 16, 8192, 8192, 1, 3)
     assert res.split_k > 1 and res.device_error == 0
     assert res.implementation.decode().endswith("splitk")
+    res = _native.gemm_run("bfloat16", 4096, 4096, 4096, 1, 3)
+    assert res.split_k == 1 and res.implementation.decode() == "tcgen05_1cta_128x256"
+    res = _native.gemm_run("float8_e4m3fn", 4096, 4096, 4096, 1, 3)
+    assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x256"
 
 
 @pytest.mark.parametrize("m", [16, 128])
