@@ -203,6 +203,28 @@ int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b
 int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
                        float scale_a, float scale_b, const trb_gemm_options* options, void* stream);
 
+/* The split-K GEMM of trb_gemm_launch (single-CTA kernel, row-major B) for
+ * callers that cannot let a library allocate device memory -- e.g. a host
+ * framework whose caching allocator already holds nearly all of HBM, or a
+ * latency-critical path that cannot absorb the synchronisation cudaMalloc /
+ * cudaFree may imply.  It calls no cudaMalloc, cudaFree or allocating library
+ * routine: its scratch (per-tile counters and fp32 partials) is one fixed
+ * array in the library's device data, 16 KiB + 16 MiB, which every GPU that
+ * loads the library holds until the process exits.
+ *  - Limit: at most 128 tile-splits of 128 x 256 (e.g. M <= 128 with
+ *    N * splits <= 32768) and 4096 output tiles; larger requests return
+ *    TRB_ERR_ARGS with the sizes in trb_last_error().  splits = 0 picks the
+ *    split count as trb_gemm_launch does (1 = no scratch used).
+ *  - The first call on a device resolves the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array and it keeps the last call's contents
+ *    (the counters are cleared by every call); calls that overlap on the GPU
+ *    (other streams, other threads) race.
+ * No counterpart in the reference: its GEMM executables own all their memory. */
+int trb_gemm_launch_noalloc(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
+                            float scale_a, float scale_b, int splits, void* stream);
+
 /* Same GEMM over HOST arrays (copies in and out inside the call). */
 int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host, const void* b_host, void* c_host,
                   float scale_a, float scale_b, int device_id, trb_result* out);

@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "trb_gemm_run",
     "trb_gemm_launch",
     "trb_gemm_launch_ex",
+    "trb_gemm_launch_noalloc",
     "trb_gemm_host",
     "trb_round_tf32",
 )
@@ -162,6 +163,8 @@ def load() -> ctypes.CDLL:
     lib.trb_gemm_launch.restype = i32
     lib.trb_gemm_launch_ex.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, ctypes.POINTER(GemmOptions), vp]
     lib.trb_gemm_launch_ex.restype = i32
+    lib.trb_gemm_launch_noalloc.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, i32, vp]
+    lib.trb_gemm_launch_noalloc.restype = i32
     lib.trb_gemm_host.argtypes = [i32, i32, i32, i32, vp, vp, vp, flt, flt, i32, res_p]
     lib.trb_gemm_host.restype = i32
     lib.trb_round_tf32.argtypes = [vp, u64, vp]
@@ -225,6 +228,14 @@ def gemm_launch_ex(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, s
     opts = GemmOptions(splits, cta_pair, B_LAYOUTS[b_layout], 0)
     check(load().trb_gemm_launch_ex(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, ctypes.byref(opts),
                                     stream or None))
+
+
+def gemm_launch_noalloc(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,
+                        scale_b: float = 1.0, splits: int = 0, stream: int = 0) -> None:
+    """Split-K GEMM whose scratch is a fixed array in the library (no device
+    allocation); see trb_gemm_launch_noalloc in include/trb_b200.h."""
+    check(load().trb_gemm_launch_noalloc(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, splits,
+                                         stream or None))
 
 
 def gemm_host(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,

@@ -959,6 +959,127 @@ int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c
     }
 }
 
+// ------------------------------------------------------------------ no-allocation split-K
+// Some callers cannot let a library call cudaMalloc: a host framework whose
+// caching allocator has already reserved nearly all of HBM (a library
+// cudaMalloc would then fail, or fragment memory the framework manages), or a
+// latency-critical path that cannot absorb the device-wide synchronisation
+// cudaMalloc / cudaFree may imply.  trb_gemm_launch_noalloc serves them: the
+// same single-CTA split-K kernel as trb_gemm_launch, with its scratch (the
+// per-tile arrival counters and the fp32 partials) in one fixed-size array in
+// the library's device data instead of the grow-only cudaMalloc'd workspace.
+// Each GPU that loads the library holds this array until the process exits.
+constexpr size_t kNoAllocCounterBytes = 16u << 10;            // 4096 per-tile counters
+constexpr size_t kNoAllocPartialBytes = 16u << 20;            // 16 MiB = 128 units of 128 x 256 fp32
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocScratch {
+    bool ready = false;
+    unsigned int* counters = nullptr;
+    float* partials = nullptr;
+};
+static NoAllocScratch g_noalloc_scratch_ptr[64];
+static std::mutex g_noalloc_mu;
+
+// Host code cannot use g_noalloc_scratch's name as a device address (it names
+// a host-side shadow); the device address comes from cudaGetSymbolAddress,
+// resolved once per device while that device is current.
+static int noalloc_scratch(int dev, NoAllocScratch* out) {
+    if (dev < 0 || dev >= 64) {
+        set_error("trb_gemm_launch_noalloc: device id %d out of range", dev);
+        return TRB_ERR_ARGS;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocScratch& s = g_noalloc_scratch_ptr[dev];
+    if (!s.ready) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            set_error("trb_gemm_launch_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+            return TRB_ERR_CUDA;
+        }
+        s.counters = static_cast<unsigned int*>(p);
+        s.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(p) + kNoAllocCounterBytes);
+        s.ready = true;
+    }
+    *out = s;
+    return TRB_OK;
+}
+
+template <int DT>
+static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale,
+                                int splits, cudaStream_t stream) {
+    using Tr = Traits<DT>;
+    constexpr int es = Tr::kEsize;
+    int dev = 0;
+    TRB_CUDA(cudaGetDevice(&dev));
+    const int sms = device_sm_count(dev);
+    const long tiles = (long)((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+    const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
+    if (splits <= 0) splits = choose_splits(tiles, num_kb, sms);
+    splits = std::max(1, std::min(splits, num_kb));
+    const int kbps = (num_kb + splits - 1) / splits;
+    splits = (num_kb + kbps - 1) / kbps;
+    const size_t partial_bytes = (size_t)tiles * splits * kBM * kBN * sizeof(float);
+    const size_t counter_bytes = (size_t)tiles * sizeof(unsigned int);
+    if (splits > 1 && (partial_bytes > kNoAllocPartialBytes || counter_bytes > kNoAllocCounterBytes)) {
+        set_error("trb_gemm_launch_noalloc: %dx%dx%d with %d K splits needs %zu bytes of split-K partials and %zu "
+                  "bytes of counters; the fixed scratch holds %zu and %zu (at most 128 tile-splits of 128 x 256)",
+                  m, n, k, splits, partial_bytes, counter_bytes, kNoAllocPartialBytes, kNoAllocCounterBytes);
+        return TRB_ERR_ARGS;
+    }
+    NoAllocScratch scratch;
+    int rc = noalloc_scratch(dev, &scratch);
+    if (rc != TRB_OK) return rc;
+    CUtensorMap tmA, tmB;
+    rc = encode_2d(&tmA, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TRB_OK) return rc;
+    rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
+    if (rc != TRB_OK) return rc;
+    TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kSmemBytes));
+    SplitK sk{splits, kbps, nullptr, nullptr};
+    if (splits > 1) {
+        // The array keeps the previous call's contents: counters must start at zero.
+        TRB_CUDA(cudaMemsetAsync(scratch.counters, 0, counter_bytes, stream));
+        sk.ws = scratch.partials;
+        sk.counters = scratch.counters;
+    }
+    const long units = tiles * splits;
+    const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
+    gemm_tcgen05_kernel<DT, false><<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, c, m, n, k, out_scale, sk);
+    TRB_CUDA(cudaGetLastError());
+    return TRB_OK;
+}
+
+static int launch_noalloc(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a,
+                          float scale_b, int splits, cudaStream_t stream) {
+    if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || b == nullptr || c == nullptr || splits < 0) {
+        set_error("trb_gemm_launch_noalloc: dimensions must be positive, pointers non-null, splits >= 0");
+        return TRB_ERR_ARGS;
+    }
+    const size_t es = dtype_size(dtype);
+    if (!(dtype == TRB_BFLOAT16 || dtype == TRB_FLOAT16 || dtype == TRB_TFLOAT32 || dtype == TRB_FLOAT8_E4M3FN ||
+          dtype == TRB_INT8)) {
+        set_error("unsupported dtype for native MFU kernel: %s", dtype_name(dtype));
+        return TRB_SKIPPED;
+    }
+    if (((size_t)k * es) % 16 != 0 || ((size_t)n * es) % 16 != 0 ||
+        ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15u)) {
+        set_error("trb_gemm_launch_noalloc: k*elem and n*elem must be multiples of 16 bytes and A, B, C 16-byte aligned");
+        return TRB_ERR_ALIGN;
+    }
+    switch (dtype) {
+        case TRB_BFLOAT16: return launch_noalloc_typed<TRB_BFLOAT16>(m, n, k, a, b, c, 1.0f, splits, stream);
+        case TRB_FLOAT16: return launch_noalloc_typed<TRB_FLOAT16>(m, n, k, a, b, c, 1.0f, splits, stream);
+        case TRB_TFLOAT32: return launch_noalloc_typed<TRB_TFLOAT32>(m, n, k, a, b, c, 1.0f, splits, stream);
+        case TRB_FLOAT8_E4M3FN:
+            return launch_noalloc_typed<TRB_FLOAT8_E4M3FN>(m, n, k, a, b, c, scale_a * scale_b, splits, stream);
+        default: return launch_noalloc_typed<TRB_INT8>(m, n, k, a, b, c, 1.0f, splits, stream);
+    }
+}
+
 // ------------------------------------------------------------------ inputs
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z += 0x9E3779B97F4A7C15ull;
@@ -1096,4 +1217,11 @@ extern "C" int trb_round_tf32(void* data, uint64_t count, void* stream) {
         static_cast<uint32_t*>(data), count);
     TRB_CUDA(cudaGetLastError());
     return TRB_OK;
+}
+
+extern "C" int trb_gemm_launch_noalloc(int dtype, int m, int n, int k, const void* a, const void* b, void* c,
+                                       float scale_a, float scale_b, int splits, void* stream) {
+    trb::clear_error();
+    return trb::gemm::launch_noalloc(dtype, m, n, k, a, b, c, scale_a, scale_b, splits,
+                                     static_cast<cudaStream_t>(stream));
 }
