@@ -195,8 +195,9 @@ int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b
  *            tiles leave more than half of the tile workers idle (e.g. the
  *            skinny M = 16 / 128 shapes).
  *  cta_pair: the CTA-pair kernel (tcgen05.mma.cta_group::2, 256 x 256 tiles)
- *            or the single-CTA kernel (128 x 256 tiles); automatic = the pair
- *            for 8-bit inputs, one CTA for 16/32-bit inputs.
+ *            or the single-CTA kernel (128 x 256 tiles); automatic = the pair,
+ *            except for skinny problems (M <= 128 with few tiles), which use
+ *            narrow single-CTA tiles (128 x 64; 128 x 128 for 8-bit row-major B).
  *  b_layout: TRB_B_K_MAJOR reads b as B^T (row-major N x K).
  * No reference counterpart: the reference's native GEMM has one tile shape
  * and no split-K (mfu_gemm_lowp.hip.hpp:423-431). */

@@ -52,6 +52,20 @@ constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
 constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBStage) + 1024;  // + alignment slack
 
+// Single-CTA tile-width variants: BN = 256 (default), 128 and 64 (skinny
+// problems: M <= 128 gives one row of tiles, so a narrow N tile is what puts
+// every SM to work).  The ring is as deep as the 227 KiB of shared memory
+// allows; TMEM holds two BN-column accumulators.
+template <int BN>
+struct TileCfg {
+    static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
+    static constexpr int kBStage = BN * kBKBytes;
+    static constexpr int kStageBytes = kAStage + kBStage;
+    static constexpr int kStages = (210 * 1024) / kStageBytes > 8 ? 8 : (210 * 1024) / kStageBytes;
+    static constexpr int kTmemCols = kNumAcc * BN;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+};
+
 // Instruction descriptor (kind::f16 / tf32 / f8f6f4 / i8): D format, A/B formats,
 // A K-major (bit 15 = 0), B MN-major (bit 16 = 1), N >> 3 at [17,23), M >> 4 at [24,29).
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt) {
@@ -60,6 +74,10 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt
 }
 // Same descriptor with B switched to K-major (bit 16 cleared).
 __host__ __device__ constexpr uint32_t idesc_b_kmajor(uint32_t idesc) { return idesc & ~(1u << 16); }
+// Same descriptor with instruction N = n (bits [17,23) hold N >> 3).
+__host__ __device__ constexpr uint32_t idesc_with_n(uint32_t idesc, int n) {
+    return (idesc & ~(0x3Fu << 17)) | ((uint32_t)(n >> 3) << 17);
+}
 
 // Per-input-type traits.  kind: 0 f16, 1 tf32, 2 f8f6f4, 3 i8.
 // B (MN-major) smem layout: 128-byte swizzle with 16-byte atoms (descriptor
@@ -197,25 +215,38 @@ struct SplitK {
     int kb_per_split;
     float* ws;
     unsigned int* counters;
+    int rotate_k;  // 1: start each tile's K loop at k-block (tile % nk) and wrap
 };
+
+// K order of a unit: with rotate_k, tiles that run at the same time start at
+// different k-blocks, so CTAs sharing one A panel (a single row of tiles,
+// M <= 128) do not all request the same A tile from the same L2 slices at
+// once.  Each tile always uses the same order, so results stay deterministic.
+__device__ __forceinline__ int k_rotation(const SplitK& sk, int tile, int nk) {
+    return sk.rotate_k && nk > 0 ? tile % nk : 0;
+}
 
 // KB: B is stored K-major (N x K row-major, "B transposed"); otherwise B is
 // the row-major K x N matrix, an MN-major operand.
-template <int DT, bool KB>
+template <int DT, bool KB, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
     using Tr = Traits<DT>;
     constexpr int kBKElems = kBKBytes / Tr::kEsize;         // K elements per stage
     constexpr int kBoxN = 128 / Tr::kEsize;                 // N elements per B box (one swizzle row)
-    constexpr int kBBoxes = kBN / kBoxN;                    // B boxes per stage
+    constexpr int kBBoxes = BN / kBoxN;                    // B boxes per stage
     constexpr int kBBoxBytes = kBKElems * 128;              // bytes of one B box == MN-atom stride (LBO)
     constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;  // K rows of B per instruction
-    constexpr uint32_t kIdesc1 = KB ? idesc_b_kmajor(Tr::kIdesc) : Tr::kIdesc;
+    using Cfg = TileCfg<BN>;
+    constexpr int kStagesT = Cfg::kStages;
+    constexpr int kBStageT = Cfg::kBStage;
+    constexpr uint32_t kIdesc1 = idesc_with_n(KB ? idesc_b_kmajor(Tr::kIdesc) : Tr::kIdesc, BN);
+    static_assert(KB || BN >= kBoxN, "MN-major B needs at least one 128-byte swizzle row per tile");
 
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[kStages];
-    __shared__ __align__(8) uint64_t empty_bar[kStages];
+    __shared__ __align__(8) uint64_t full_bar[kStagesT];
+    __shared__ __align__(8) uint64_t empty_bar[kStagesT];
     __shared__ __align__(8) uint64_t accf_bar[kNumAcc];
     __shared__ __align__(8) uint64_t acce_bar[kNumAcc];
     __shared__ __align__(8) uint64_t drain_bar;
@@ -225,18 +256,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = smem_base;
-    const uint32_t sB = smem_base + kStages * kAStage;
+    const uint32_t sB = smem_base + kStagesT * kAStage;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_m = (M + kBM - 1) / kBM;
-    const int num_n = (N + kBN - 1) / kBN;
+    const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + kBKElems - 1) / kBKElems;
     const int num_units = num_tiles * sk.splits;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kStagesT; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), 1);
         }
@@ -251,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 0) {
-        tmem_alloc(smem_u32(&tmem_slot), kTmemCols);
+        tmem_alloc(smem_u32(&tmem_slot), Cfg::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -269,8 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int mb, nb;
                 tile_coords(unit / sk.splits, num_m, num_n, mb, nb);
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
-                const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
-                for (int kb = kb0; kb < kb1; ++kb) {
+                const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
+                const int rot = k_rotation(sk, unit / sk.splits, nk);
+                for (int i = 0; i < nk; ++i) {
+                    const int kb = kb0 + (i + rot < nk ? i + rot : i + rot - nk);
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrProducerWait);
                         abort_flag = 1;
@@ -278,26 +311,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
-                    mbar_arrive_expect_tx(fb, kAStage + kBStage);
+                    mbar_arrive_expect_tx(fb, kAStage + kBStageT);
                     tma_load_2d(sA + stage * kAStage, &tmA, fb, kb * kBKElems, mb * kBM);
                     if constexpr (KB) {
-                        tma_load_2d(sB + stage * kBStage, &tmB, fb, kb * kBKElems, nb * kBN);
+                        tma_load_2d(sB + stage * kBStageT, &tmB, fb, kb * kBKElems, nb * BN);
                     } else {
 #pragma unroll
                         for (int j = 0; j < kBBoxes; ++j)
-                            tma_load_2d(sB + stage * kBStage + j * kBBoxBytes, &tmB, fb, nb * kBN + j * kBoxN,
+                            tma_load_2d(sB + stage * kBStageT + j * kBBoxBytes, &tmB, fb, nb * BN + j * kBoxN,
                                         kb * kBKElems);
                     }
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-                    if (++stage == kStages) {
+                    if (++stage == kStagesT) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
             }
             // Drain: the CTA must not exit while a TMA write into its smem is pending.
-            for (int s = 0; s < kStages; ++s)
+            for (int s = 0; s < kStagesT; ++s)
                 if (issued_mask & (1u << s))
                     if (!mbar_wait(smem_u32(&full_bar[s]), (issued_phase >> s) & 1u, nullptr))
                         atomicCAS(&g_gemm_error, 0, kErrDrainWait);
@@ -315,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int t_local = 0;
             for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++t_local) {
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
-                const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
+                const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
                 const int acc = t_local & 1;
                 const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
                 if (!mbar_wait(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
@@ -324,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
-                for (int kb = kb0; kb < kb1; ++kb) {
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int i = 0; i < nk; ++i) {  // same (rotated) order as the producer; only the count matters here
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
@@ -335,14 +368,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // TMA completion is ordered before the MMA by the barrier's
                     // transaction count: no tcgen05 fence is needed per k-block.
                     const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kAStage) >> 4);
-                    const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kBStage) >> 4);
+                    const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kBStageT) >> 4);
 #pragma unroll
                     for (int ks = 0; ks < kKSteps; ++ks)
                         mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kInstrKBytes >> 4),
                                        b_stage + (uint64_t)(ks * kBKStep >> 4), kIdesc1,
-                                       (kb != kb0 || ks != 0) ? 1u : 0u);
+                                       (i != 0 || ks != 0) ? 1u : 0u);
                     tc_commit(smem_u32(&empty_bar[stage]));  // frees the smem stage when these MMAs finish
-                    if (++stage == kStages) {
+                    if (++stage == kStagesT) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -377,14 +410,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const int grow = mb * kBM + row_in_tile;
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
             if (sk.splits == 1) {
 #pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
+                for (int c = 0; c < BN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
                     tmem_wait_ld();
-                    const int gcol = nb * kBN + c * 32;
+                    const int gcol = nb * BN + c * 32;
                     if (grow < M && gcol < N) store_chunk<DT>(C, grow, gcol, N, r, out_scale);
                 }
                 tc_fence_before();
@@ -393,13 +426,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
             // ---- split-K: publish this unit's fp32 partial
-            float* wrow = sk.ws + ((size_t)unit * kBM + row_in_tile) * kBN;
+            float* wrow = sk.ws + ((size_t)unit * kBM + row_in_tile) * BN;
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
                 tmem_wait_ld();
-                if (grow < M && nb * kBN + c * 32 < N) {
+                if (grow < M && nb * BN + c * 32 < N) {
                     uint4* w4 = reinterpret_cast<uint4*>(wrow + c * 32);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) w4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
@@ -417,10 +450,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- last arrival: deterministic sum over splits 0..S-1, convert, store C
             __threadfence();
             if (grow < M) {
-                const float* base = sk.ws + ((size_t)tile * sk.splits * kBM + row_in_tile) * kBN;
+                const float* base = sk.ws + ((size_t)tile * sk.splits * kBM + row_in_tile) * BN;
 #pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    const int gcol = nb * kBN + c * 32;
+                for (int c = 0; c < BN / 32; ++c) {
+                    const int gcol = nb * BN + c * 32;
                     if (gcol >= N) break;
                     float acc_f[32];
                     const float4* p0 = reinterpret_cast<const float4*>(base + c * 32);
@@ -430,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
                     }
                     for (int sp = 1; sp < sk.splits; ++sp) {
-                        const float4* ps = reinterpret_cast<const float4*>(base + (size_t)sp * kBM * kBN + c * 32);
+                        const float4* ps = reinterpret_cast<const float4*>(base + (size_t)sp * kBM * BN + c * 32);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const float4 v = __ldcg(ps + i);
@@ -458,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
 }
 
@@ -850,6 +883,45 @@ static int choose_splits(long tiles, int num_kb, int sms) {
     return (int)std::max<long>(1, std::min<long>(s, 16));
 }
 
+// Narrowest single-CTA tile width for skinny problems: one row of 128-row
+// tiles that, at BN = 256, would leave more than half of the SMs idle.  8-bit
+// MN-major B needs BN >= 128 (one 128-byte swizzle row holds 128 elements).
+static int choose_tile_n(int m, int n, int es, bool kb, int sms) {
+    const long tiles256 = (long)((m + kBM - 1) / kBM) * ((n + 255) / 256);
+    if (m > kBM || tiles256 * 2 > sms) return 256;
+    return (es >= 2 || kb) ? 64 : 128;
+}
+
+template <int DT, bool KB, int BN>
+static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, int n, int k, void* c,
+                         float out_scale, int splits, int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
+    using Tr = Traits<DT>;
+    using Cfg = TileCfg<BN>;
+    static bool attr_set[64] = {};
+    if (dev < 64 && !attr_set[dev]) {
+        TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, KB, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)Cfg::kSmem));
+        attr_set[dev] = true;
+    }
+    const long tiles = (long)((m + kBM - 1) / kBM) * ((n + BN - 1) / BN);
+    const int num_kb = (int)(((long)k * Tr::kEsize + kBKBytes - 1) / kBKBytes);
+    if (splits <= 0) splits = choose_splits(tiles, num_kb, sms);
+    splits = std::max(1, std::min(splits, num_kb));
+    const int kbps = (num_kb + splits - 1) / splits;
+    splits = (num_kb + kbps - 1) / kbps;  // every split owns at least one k-block
+    SplitK sk{splits, kbps, nullptr, nullptr, m <= kBM ? 1 : 0};
+    if (splits > 1) {
+        const int rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * BN * sizeof(float), (size_t)tiles, &sk);
+        if (rc != TRB_OK) return rc;
+    }
+    const long units = tiles * splits;
+    const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
+    gemm_tcgen05_kernel<DT, KB, BN><<<grid, kThreads, Cfg::kSmem, stream>>>(tmA, tmB, c, m, n, k, out_scale, sk);
+    TRB_CUDA(cudaGetLastError());
+    if (info) *info = {grid, kThreads, splits, 0, BN};
+    return TRB_OK;
+}
+
 template <int DT, bool KB>
 static int launch_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale, int splits,
                         int cta_pair, cudaStream_t stream, LaunchInfo* info) {
@@ -858,57 +930,56 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     int dev = 0;
     TRB_CUDA(cudaGetDevice(&dev));
     const int sms = device_sm_count(dev);
-    // Automatic choice, from sustained clock-normalised measurements on B200:
-    // the CTA pair for 8-bit inputs (e4m3 / int8: +3% over one CTA), one CTA
-    // for 16/32-bit inputs (bf16 8192^3: 78.7% vs 77.6% of the per-clock peak).
-    const bool pair = (cta_pair > 0 || (cta_pair < 0 && es == 1)) && sms >= 2;
-    const int tile_m = pair ? kPairM : kBM;
-    const int tile_n = pair ? kPairN : kBN;
-    const int slots_per_unit = pair ? 2 : 1;
-    const int workers = pair ? sms / 2 : sms;  // independent tile workers (pairs or CTAs)
+    // Automatic choice, from sustained clock-normalised measurements on B200
+    // (8192^3, TFLOP/s per SM-GHz): the CTA pair (bf16 96%, e4m3 90% of the
+    // per-clock tensor peak, vs 83% / 79% for one CTA), except for skinny
+    // problems, which take narrow single-CTA tiles.
+    const int tile_n_single = choose_tile_n(m, n, es, KB, sms);
+    const bool pair = (cta_pair > 0 || (cta_pair < 0 && tile_n_single == 256)) && sms >= 2;
+    const int tile_n = pair ? kPairN : tile_n_single;
 
     CUtensorMap tmA, tmB;
     int rc = encode_2d(&tmA, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != TRB_OK) return rc;
     if (KB)  // B^T: N rows of K elements, boxes of (128-byte K slice) x (tile N rows)
-        rc = encode_2d(&tmB, b, es, (uint64_t)k, (uint64_t)n, kBKBytes / es, pair ? kHalfN : kBN,
+        rc = encode_2d(&tmB, b, es, (uint64_t)k, (uint64_t)n, kBKBytes / es, pair ? kHalfN : tile_n,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     else
         rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
-    static bool attr_set[64][2] = {};  // per template instance
-    if (dev < 64 && !attr_set[dev][pair]) {
-        if (pair)
-            TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_pair_kernel<DT, KB>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes));
-        else
-            TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)kSmemBytes));
-        attr_set[dev][pair] = true;
+    if (!pair) {
+        if (tile_n == 64) {
+            if constexpr (KB || es >= 2)
+                return launch_single<DT, KB, 64>(tmA, tmB, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        } else if (tile_n == 128) {
+            return launch_single<DT, KB, 128>(tmA, tmB, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        }
+        return launch_single<DT, KB, 256>(tmA, tmB, m, n, k, c, out_scale, splits, dev, sms, stream, info);
     }
-    const long tiles = (long)((m + tile_m - 1) / tile_m) * ((n + tile_n - 1) / tile_n);
+    static bool attr_set[64] = {};
+    if (dev < 64 && !attr_set[dev]) {
+        TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_pair_kernel<DT, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kPairSmemBytes));
+        attr_set[dev] = true;
+    }
+    const int workers = sms / 2;
+    const long tiles = (long)((m + kPairM - 1) / kPairM) * ((n + kPairN - 1) / kPairN);
     const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
     if (splits <= 0) splits = choose_splits(tiles, num_kb, workers);
     splits = std::max(1, std::min(splits, num_kb));
     const int kbps = (num_kb + splits - 1) / splits;
-    splits = (num_kb + kbps - 1) / kbps;  // every split owns at least one k-block
-    SplitK sk{splits, kbps, nullptr, nullptr};
+    splits = (num_kb + kbps - 1) / kbps;
+    SplitK sk{splits, kbps, nullptr, nullptr, 0};
     if (splits > 1) {
-        rc = ensure_workspace(dev, (size_t)tiles * splits * slots_per_unit * kBM * tile_n * sizeof(float),
-                              (size_t)tiles * slots_per_unit, &sk);
+        rc = ensure_workspace(dev, (size_t)tiles * splits * 2 * kBM * kPairN * sizeof(float), (size_t)tiles * 2, &sk);
         if (rc != TRB_OK) return rc;
     }
     const long units = tiles * splits;
     const int grid_workers = (int)std::max<long>(1, std::min<long>(units, workers));
-    if (pair) {
-        gemm_tcgen05_pair_kernel<DT, KB><<<grid_workers * 2, kThreads, kPairSmemBytes, stream>>>(tmA, tmB, c, m, n,
-                                                                                              k, out_scale, sk);
-    } else {
-        gemm_tcgen05_kernel<DT, KB><<<grid_workers, kThreads, kSmemBytes, stream>>>(tmA, tmB, c, m, n, k, out_scale,
-                                                                                    sk);
-    }
+    gemm_tcgen05_pair_kernel<DT, KB><<<grid_workers * 2, kThreads, kPairSmemBytes, stream>>>(tmA, tmB, c, m, n, k,
+                                                                                          out_scale, sk);
     TRB_CUDA(cudaGetLastError());
-    if (info) *info = {pair ? grid_workers * 2 : grid_workers, kThreads, splits, pair ? 1 : 0};
+    if (info) *info = {grid_workers * 2, kThreads, splits, 1, kPairN};
     return TRB_OK;
 }
 
@@ -1037,9 +1108,9 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     if (rc != TRB_OK) return rc;
     rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
-    TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)kSmemBytes));
-    SplitK sk{splits, kbps, nullptr, nullptr};
+    TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)TileCfg<256>::kSmem));
+    SplitK sk{splits, kbps, nullptr, nullptr, 0};
     if (splits > 1) {
         // The array keeps the previous call's contents: counters must start at zero.
         TRB_CUDA(cudaMemsetAsync(scratch.counters, 0, counter_bytes, stream));
@@ -1048,7 +1119,8 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     }
     const long units = tiles * splits;
     const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
-    gemm_tcgen05_kernel<DT, false><<<grid, kThreads, kSmemBytes, stream>>>(tmA, tmB, c, m, n, k, out_scale, sk);
+    gemm_tcgen05_kernel<DT, false, 256><<<grid, kThreads, TileCfg<256>::kSmem, stream>>>(tmA, tmB, c, m, n, k,
+                                                                                         out_scale, sk);
     TRB_CUDA(cudaGetLastError());
     return TRB_OK;
 }

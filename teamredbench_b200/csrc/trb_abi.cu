@@ -400,8 +400,8 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
     out->blocks_per_sm = 1;
     out->split_k = info.splits;
     out->launches = args->iterations;
-    snprintf(out->implementation, sizeof(out->implementation), "%s%s",
-             info.pair ? "tcgen05_cta_pair_256x256" : "tcgen05_1cta_128x256", info.splits > 1 ? "_splitk" : "");
+    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_%s_%dx%d%s", info.pair ? "cta_pair" : "1cta",
+             info.pair ? 256 : 128, info.tile_n, info.splits > 1 ? "_splitk" : "");
     return check_device_errors(out);
 }
 
@@ -475,7 +475,7 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     out->grid = info.grid;
     out->block = info.block;
     out->launches = 1;
-    snprintf(out->implementation, sizeof(out->implementation), "%s+copies",
-             info.pair ? "tcgen05_cta_pair_256x256" : "tcgen05_1cta_128x256");
+    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_%s_%dx%d+copies",
+             info.pair ? "cta_pair" : "1cta", info.pair ? 256 : 128, info.tile_n);
     return check_device_errors(out);
 }
