@@ -3,7 +3,7 @@
 // PTX wrappers for mbarriers, TMA (cp.async.bulk / cp.async.bulk.tensor), and
 // the tcgen05 tensor-core / TMEM instructions, plus bounded waits and the
 // per-thread error string of the C ABI.  No TMA load here uses
-// .multicast::cluster: the kernels run replicated on 1..8 GPUs.
+// a cluster-broadcast qualifier: the kernels run replicated on 1..8 GPUs.
 #pragma once
 
 #include <cuda.h>
