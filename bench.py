@@ -265,6 +265,7 @@ def run_b200(args) -> None:
     extras = {}
     if not args.no_extras:
         extras = secondary_measurements(torch, dev, stream, peaks)
+        extras["scope"] = f"single-GPU measurements on rank {rank}"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
