@@ -109,7 +109,7 @@ typedef enum trb_b_layout {
 } trb_b_layout;
 
 typedef struct trb_gemm_args {
-    int32_t dtype;           /* BFLOAT16, FLOAT16, TFLOAT32, FLOAT8_E4M3FN or INT8 */
+    int32_t dtype;           /* BFLOAT16, FLOAT16, TFLOAT32, FLOAT8_E4M3FN, INT8, FLOAT32 or FLOAT64 */
     int32_t m, n, k;
     int32_t warmup;
     int32_t iterations;
@@ -176,11 +176,16 @@ int trb_gemm_run(const trb_gemm_args* args, trb_result* out);
 
 /* One launch: C = A * B over caller-owned device arrays, all row-major:
  * A m x k, B k x n, C m x n.  Accumulate in fp32 (int32 for int8).  Output
- * element type: bf16 for bf16 and e4m3 inputs, f16 for f16, f32 for tf32,
- * int32 for int8.  e4m3 results are multiplied by scale_a * scale_b before
- * rounding; other dtypes ignore the scales.  tf32 uses the upper 19 bits of
- * each f32 input.  Requires k * elem % 16 == 0, n * elem % 16 == 0 and
- * 16-byte aligned pointers (TMA); any m, n, k > 0 otherwise.  Replaces
+ * element type: bf16 for bf16 and e4m3 inputs, f16 for f16, f32 for tf32 and
+ * float32, f64 for float64, int32 for int8.  e4m3 results are multiplied by
+ * scale_a * scale_b before rounding; other dtypes ignore the scales.  tf32
+ * uses the upper 19 bits of each f32 input.  float32 runs on the tf32 tensor
+ * cores as three products (x = hi + lo, C = A_lo B_hi + A_hi B_lo + A_hi B_hi;
+ * one split pass per operand into a library workspace of 12 (mk + kn) bytes);
+ * float64 runs on CUDA cores (no tensor-core kind takes fp64) and needs only
+ * 8-byte aligned pointers.  Others require k * elem % 16 == 0,
+ * n * elem % 16 == 0 and 16-byte aligned pointers (TMA); any m, n, k > 0
+ * otherwise.  Replaces
  * the reference's torch.mm(a, b, out=out) (src/teamredbench/benchmarks/mfu.py:
  * 229-234) and the native mfma_gemm_*_kernel launches. */
 int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c,

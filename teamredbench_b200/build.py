@@ -25,7 +25,7 @@ LIB_DIR = PKG / "lib"
 OBJ_DIR = LIB_DIR / "obj"
 INCLUDE = ROOT / "include"
 
-CUDA_SOURCES = ["trb_abi.cu", "hbm_stream.cu", "gemm_tcgen05.cu"]
+CUDA_SOURCES = ["trb_abi.cu", "hbm_stream.cu", "gemm_tcgen05.cu", "gemm_fp64.cu"]
 HEADERS = [CSRC / "trb_common.cuh", INCLUDE / "trb_b200.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",

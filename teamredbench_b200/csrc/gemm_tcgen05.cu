@@ -983,6 +983,91 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     return TRB_OK;
 }
 
+// ------------------------------------------------------------------ float32 via 3xTF32
+// A float32 GEMM on the tf32 tensor cores, accurate to ~fp32: each input
+// x = hi + lo with hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32),
+// and C = A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (the dropped A_lo*B_lo term is
+// ~2^-22 of a product).  The three products are ONE tf32 GEMM over K' = 3K:
+//   A' = [A_lo | A_hi | A_hi]  (M x 3K),   B' = [B_hi ; B_lo ; B_hi]  (3K x N)
+// (B^T storage: rows [B_hi | B_lo | B_hi]).  The small terms come first in K,
+// so they accumulate into a small partial sum.  A' and B' live in a per-device
+// grow-only buffer of 12 (MK + KN) bytes, built by one split pass per operand
+// (the reference's float32 path is an fp32 rocWMMA kernel,
+// mfu_gemm_highp.hip.hpp:39-218; its parity tolerance for fp32 is 1e-4).
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t t;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(x));
+    return __uint_as_float(t);
+}
+
+// parts: bit j set = part j is hi, clear = lo.  `stacked`: parts are stacked
+// rows x cols blocks (dst = 3 * rows x cols); otherwise parts are concatenated
+// along each row (dst = rows x 3 * cols).  cols % 4 == 0.
+__global__ void split3_tf32_kernel(const float4* __restrict__ src, float4* __restrict__ dst, uint64_t rows,
+                                   uint64_t cols4, uint32_t parts, int stacked) {
+    const uint64_t total = rows * cols4;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float4 x = src[i];
+        float4 hi, lo;
+        hi.x = tf32_rna(x.x); lo.x = tf32_rna(x.x - hi.x);
+        hi.y = tf32_rna(x.y); lo.y = tf32_rna(x.y - hi.y);
+        hi.z = tf32_rna(x.z); lo.z = tf32_rna(x.z - hi.z);
+        hi.w = tf32_rna(x.w); lo.w = tf32_rna(x.w - hi.w);
+        const uint64_t r = i / cols4, c = i - r * cols4;
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const uint64_t o = stacked ? (uint64_t)part * total + i : r * 3 * cols4 + (uint64_t)part * cols4 + c;
+            dst[o] = (parts >> part) & 1u ? hi : lo;
+        }
+    }
+}
+
+struct Fp32x3Workspace {
+    float* buf = nullptr;
+    size_t bytes = 0;
+    std::mutex mu;
+};
+static Fp32x3Workspace g_fp32x3[64];
+
+static int launch_fp32x3(int m, int n, int k, const void* a, const void* b, void* c, int splits, int cta_pair,
+                         int b_kmajor, cudaStream_t stream, LaunchInfo* info) {
+    int dev = 0;
+    TRB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) {
+        set_error("device id %d out of range", dev);
+        return TRB_ERR_ARGS;
+    }
+    const size_t a3 = (size_t)m * k * 3, b3 = (size_t)k * n * 3;
+    Fp32x3Workspace& w = g_fp32x3[dev];
+    std::lock_guard<std::mutex> lock(w.mu);
+    if (w.bytes < (a3 + b3) * sizeof(float)) {
+        if (w.buf) cudaFree(w.buf);
+        w.buf = nullptr;
+        w.bytes = 0;
+        TRB_CUDA(cudaMalloc(&w.buf, (a3 + b3) * sizeof(float)));
+        w.bytes = (a3 + b3) * sizeof(float);
+    }
+    float* ap = w.buf;
+    float* bp = w.buf + a3;  // a3 * 4 bytes is a multiple of 16 (k % 4 == 0)
+    const int grid = device_sm_count(dev) * 8;
+    constexpr uint32_t kLoHiHi = 0b110, kHiLoHi = 0b101;
+    split3_tf32_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4*>(a), reinterpret_cast<float4*>(ap),
+                                                 (uint64_t)m, (uint64_t)k / 4, kLoHiHi, 0);
+    TRB_CUDA(cudaGetLastError());
+    if (b_kmajor)  // B^T rows (N x K) -> N x 3K
+        split3_tf32_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4*>(b), reinterpret_cast<float4*>(bp),
+                                                     (uint64_t)n, (uint64_t)k / 4, kHiLoHi, 0);
+    else  // row-major K x N -> 3K x N
+        split3_tf32_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4*>(b), reinterpret_cast<float4*>(bp),
+                                                     (uint64_t)k, (uint64_t)n / 4, kHiLoHi, 1);
+    TRB_CUDA(cudaGetLastError());
+    const int rc = b_kmajor ? launch_typed<TRB_TFLOAT32, true>(m, n, 3 * k, ap, bp, c, 1.0f, splits, cta_pair, stream, info)
+                            : launch_typed<TRB_TFLOAT32, false>(m, n, 3 * k, ap, bp, c, 1.0f, splits, cta_pair, stream,
+                                                                info);
+    if (info) info->fp32x3 = 1;
+    return rc;
+}
+
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
            int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info) {
     if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || b == nullptr || c == nullptr) {
@@ -991,10 +1076,11 @@ int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c
     }
     const size_t es = dtype_size(dtype);
     if (!(dtype == TRB_BFLOAT16 || dtype == TRB_FLOAT16 || dtype == TRB_TFLOAT32 || dtype == TRB_FLOAT8_E4M3FN ||
-          dtype == TRB_INT8)) {
+          dtype == TRB_INT8 || dtype == TRB_FLOAT32 || dtype == TRB_FLOAT64)) {
         set_error("unsupported dtype for native MFU kernel: %s", dtype_name(dtype));
         return TRB_SKIPPED;
     }
+    if (dtype == TRB_FLOAT64) return dgemm::launch(m, n, k, a, b, c, b_kmajor, stream, info);
     if (((size_t)k * es) % 16 != 0 || ((size_t)n * es) % 16 != 0) {
         set_error("trb_gemm_launch: k*elem and n*elem must be multiples of 16 bytes (k=%d n=%d elem=%zu)", k, n, es);
         return TRB_ERR_ALIGN;
@@ -1008,6 +1094,7 @@ int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c
         set_error("trb_gemm_launch: splits must be >= 0");
         return TRB_ERR_ARGS;
     }
+    if (dtype == TRB_FLOAT32) return launch_fp32x3(m, n, k, a, b, c, splits, cta_pair, b_kmajor, stream, info);
     if (b_kmajor) {
         switch (dtype) {
             case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
@@ -1187,6 +1274,8 @@ __global__ void fill_gemm_kernel(void* data, int dtype, uint64_t n, uint64_t see
             case TRB_FLOAT16:
                 static_cast<__half*>(data)[i] = __float2half_rn(normal_scaled(seed, i, inv_sqrt_k));
                 break;
+            case TRB_FLOAT32: static_cast<float*>(data)[i] = normal_scaled(seed, i, inv_sqrt_k); break;
+            case TRB_FLOAT64: static_cast<double*>(data)[i] = (double)normal_scaled(seed, i, inv_sqrt_k); break;
             case TRB_TFLOAT32: {
                 uint32_t t;
                 asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(normal_scaled(seed, i, inv_sqrt_k)));

@@ -327,11 +327,21 @@ extern "C" int trb_hbm_host(int dtype, int mode, void* dst_host, const void* src
 
 static bool gemm_dtype_supported(int dtype) {
     return dtype == TRB_BFLOAT16 || dtype == TRB_FLOAT16 || dtype == TRB_TFLOAT32 || dtype == TRB_FLOAT8_E4M3FN ||
-           dtype == TRB_INT8;
+           dtype == TRB_INT8 || dtype == TRB_FLOAT32 || dtype == TRB_FLOAT64;
 }
 
 static size_t gemm_out_size(int dtype) {
-    return (dtype == TRB_TFLOAT32 || dtype == TRB_INT8) ? 4 : 2;
+    if (dtype == TRB_FLOAT64) return 8;
+    return (dtype == TRB_TFLOAT32 || dtype == TRB_INT8 || dtype == TRB_FLOAT32) ? 4 : 2;
+}
+
+static void gemm_impl_name(const gemm::LaunchInfo& info, char* out, size_t size, const char* suffix) {
+    if (info.fp64) {
+        snprintf(out, size, "fp64_fma_128x128%s", suffix);
+        return;
+    }
+    snprintf(out, size, "%stcgen05_%s_%dx%d%s%s", info.fp32x3 ? "fp32x3_" : "", info.pair ? "cta_pair" : "1cta",
+             info.pair ? 256 : 128, info.tile_n, info.splits > 1 ? "_splitk" : "", suffix);
 }
 
 extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
@@ -399,9 +409,8 @@ extern "C" int trb_gemm_run(const trb_gemm_args* args, trb_result* out) {
     out->block = info.block;
     out->blocks_per_sm = 1;
     out->split_k = info.splits;
-    out->launches = args->iterations;
-    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_%s_%dx%d%s", info.pair ? "cta_pair" : "1cta",
-             info.pair ? 256 : 128, info.tile_n, info.splits > 1 ? "_splitk" : "");
+    out->launches = args->iterations * (info.fp32x3 ? 3 : 1);
+    gemm_impl_name(info, out->implementation, sizeof(out->implementation), "");
     return check_device_errors(out);
 }
 
@@ -475,7 +484,6 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     out->grid = info.grid;
     out->block = info.block;
     out->launches = 1;
-    snprintf(out->implementation, sizeof(out->implementation), "tcgen05_%s_%dx%d+copies",
-             info.pair ? "cta_pair" : "1cta", info.pair ? 256 : 128, info.tile_n);
+    gemm_impl_name(info, out->implementation, sizeof(out->implementation), "+copies");
     return check_device_errors(out);
 }

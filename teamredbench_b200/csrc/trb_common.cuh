@@ -47,6 +47,8 @@ int read_error(bool clear);
 namespace gemm {
 struct LaunchInfo {
     int grid = 0, block = 0, splits = 1, pair = 0, tile_n = 256;
+    int fp32x3 = 0;   // float32 computed as three tf32 products
+    int fp64 = 0;     // float64 CUDA-core kernel
 };
 // splits: 0 = automatic (split-K only for problems that leave SMs idle), >= 1 forced.
 // cta_pair: < 0 automatic (pair, or narrow single-CTA tiles when skinny), 0 single-CTA, > 0 CTA pair.
@@ -57,6 +59,12 @@ int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsign
                  float* scale_out, cudaStream_t stream);
 int read_error(bool clear);
 }  // namespace gemm
+
+namespace dgemm {
+// float64 C = A * B on CUDA cores (no tcgen05 kind takes fp64); any m, n, k.
+int launch(int m, int n, int k, const void* a, const void* b, void* c, int b_kmajor, cudaStream_t stream,
+           gemm::LaunchInfo* info);
+}  // namespace dgemm
 
 // Bounded-wait budget for every spin inside the kernels (nanoseconds of
 // %globaltimer).  A healthy wait lasts microseconds.

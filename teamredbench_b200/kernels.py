@@ -69,8 +69,10 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     With b_transposed=True, `b` holds B^T as a row-major (n x k) tensor.
 
     dtype defaults to the tensors' dtype; pass ``dtype="tfloat32"`` to run
-    float32 tensors on the tf32 tensor-core path.  Output dtypes: bf16 for
-    bf16 / e4m3 inputs, f16 for f16, f32 for tf32, int32 for int8.
+    float32 tensors on the tf32 tensor-core path (float32 itself runs as three
+    tf32 products, float64 on the CUDA cores).  Output dtypes: bf16 for bf16 /
+    e4m3 inputs, f16 for f16, f32 for tf32 and float32, f64 for float64, int32
+    for int8.
     splits: 0 = automatic split-K, >= 1 forces that many K splits.
     cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel."""
     _require_cuda_contiguous(a, b, out)

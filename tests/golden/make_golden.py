@@ -101,7 +101,8 @@ def _round_tf32(x: torch.Tensor) -> torch.Tensor:
 def make_gemm() -> dict[str, np.ndarray]:
     out: dict[str, np.ndarray] = {}
     for tag, (m, n, k) in GEMM_SHAPES.items():
-        dtypes = ("bfloat16", "float16", "tfloat32", "float8_e4m3fn", "int8") if tag == "square" else ("bfloat16",)
+        dtypes = (("bfloat16", "float16", "tfloat32", "float8_e4m3fn", "int8", "float32", "float64")
+                  if tag == "square" else ("bfloat16",))
         for dtype_name in dtypes:
             g = torch.Generator().manual_seed(0)
             key = f"{tag}/{dtype_name}"
@@ -114,7 +115,13 @@ def make_gemm() -> dict[str, np.ndarray]:
                 continue
             a32 = torch.randn(m, k, generator=g) / math.sqrt(k)
             b32 = torch.randn(k, n, generator=g) / math.sqrt(k)
-            if dtype_name in ("bfloat16", "float16"):
+            if dtype_name == "float64":
+                a = torch.randn(m, k, generator=g, dtype=torch.float64) / math.sqrt(k)
+                b = torch.randn(k, n, generator=g, dtype=torch.float64) / math.sqrt(k)
+                c = torch.empty((m, n), dtype=torch.float64)
+                torch.mm(a, b, out=c)
+                out.update({f"{key}/a": _raw(a), f"{key}/b": _raw(b), f"{key}/c": _raw(c)})
+            elif dtype_name in ("bfloat16", "float16", "float32"):
                 dt = getattr(torch, dtype_name)
                 a, b = a32.to(dt), b32.to(dt)
                 c = torch.empty((m, n), dtype=dt)

@@ -19,8 +19,12 @@ TORCH_DTYPE = {
 }
 
 GEMM_OUT = {"bfloat16": "bfloat16", "float16": "float16", "tfloat32": "float32", "float8_e4m3fn": "bfloat16",
-            "int8": "int32"}
-GEMM_TOLERANCE = {"bfloat16": 1e-2, "float16": 1e-2, "float8_e4m3fn": 1e-2, "tfloat32": 1e-5}
+            "int8": "int32", "float32": "float32", "float64": "float64"}
+# rel-to-max tolerances of the reference's native GEMM harness
+# (tests/native/gemm_parity.hip.cpp:174-178: 1e-10 for double, 1e-4 for float,
+# 1e-2 for 16-bit), tightened to 1e-5 for tf32-exact inputs.
+GEMM_TOLERANCE = {"bfloat16": 1e-2, "float16": 1e-2, "float8_e4m3fn": 1e-2, "tfloat32": 1e-5,
+                  "float32": 1e-4, "float64": 1e-10}
 # tf32 beyond K = 4096: the tensor core's fp32 accumulation over one K = 8192
 # pass gives 2.2e-5 (rel-to-max) on tf32-exact inputs -- identical to cuBLAS's
 # tf32 GEMM on the same inputs (test_baseline_8192_tf32_matches_tensor_core_accumulation).
@@ -88,9 +92,13 @@ def gemm_operands(name: str, m: int, n: int, k: int, seed: int = 0, device: str 
         a = torch.randint(-127, 128, (m, k), generator=g, device=device, dtype=torch.int8)
         b = torch.randint(-127, 128, (k, n), generator=g, device=device, dtype=torch.int8)
         return a, b, 1.0, 1.0
+    if name == "float64":
+        a = torch.randn(m, k, generator=g, device=device, dtype=torch.float64) / math.sqrt(k)
+        b = torch.randn(k, n, generator=g, device=device, dtype=torch.float64) / math.sqrt(k)
+        return a, b, 1.0, 1.0
     a32 = torch.randn(m, k, generator=g, device=device) / math.sqrt(k)
     b32 = torch.randn(k, n, generator=g, device=device) / math.sqrt(k)
-    if name in ("bfloat16", "float16"):
+    if name in ("bfloat16", "float16", "float32"):
         return a32.to(torch_dtype(name)), b32.to(torch_dtype(name)), 1.0, 1.0
     if name == "tfloat32":
         from teamredbench_b200 import _native
