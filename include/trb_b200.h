@@ -122,7 +122,8 @@ typedef struct trb_gemm_options {
     int32_t splits;          /* 0 = automatic split-K; >= 1 forces that many K splits */
     int32_t cta_pair;        /* < 0 automatic, 0 = single-CTA 128 x 256 tiles, > 0 = CTA-pair 256 x 256 tiles */
     int32_t b_layout;        /* trb_b_layout */
-    int32_t reserved;
+    int32_t tile_n;          /* 0 = automatic; 64, 128 or 256 = single-CTA kernel with tiles of that width;
+                                < 0 = swapped-operand kernel (C^T = B^T A^T, m <= 64) */
 } trb_gemm_options;
 
 /* ---- library ------------------------------------------------------------ */
@@ -201,9 +202,15 @@ int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b
  *            skinny M = 16 / 128 shapes).
  *  cta_pair: the CTA-pair kernel (tcgen05.mma.cta_group::2, 256 x 256 tiles)
  *            or the single-CTA kernel (128 x 256 tiles); automatic = the pair,
- *            except for skinny problems (M <= 128 with few tiles), which use
+ *            except for skinny problems: M <= 64 takes the swapped-operand
+ *            kernel (C^T = B^T A^T: 128 columns of C per tile, the rows of A as
+ *            the MMA's N = 16, 32 or 64), and M <= 128 with few tiles takes
  *            narrow single-CTA tiles (128 x 64; 128 x 128 for 8-bit row-major B).
  *  b_layout: TRB_B_K_MAJOR reads b as B^T (row-major N x K).
+ *  tile_n:   0 automatic; 64 / 128 / 256 force the single-CTA kernel with that
+ *            tile width (8-bit row-major B: >= 128); < 0 forces the
+ *            swapped-operand kernel (m <= 64).  Explicit cta_pair >= 0 also
+ *            turns the automatic swapped choice off.
  * No reference counterpart: the reference's native GEMM has one tile shape
  * and no split-K (mfu_gemm_lowp.hip.hpp:423-431). */
 int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void* b, void* c,

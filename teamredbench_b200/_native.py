@@ -123,7 +123,7 @@ class GemmOptions(ctypes.Structure):
         ("splits", ctypes.c_int32),
         ("cta_pair", ctypes.c_int32),
         ("b_layout", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
     ]
 
 
@@ -224,8 +224,8 @@ def gemm_launch(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scal
 
 def gemm_launch_ex(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_a: float = 1.0,
                    scale_b: float = 1.0, splits: int = 0, cta_pair: int = -1, b_layout: str = "row_major",
-                   stream: int = 0) -> None:
-    opts = GemmOptions(splits, cta_pair, B_LAYOUTS[b_layout], 0)
+                   stream: int = 0, tile_n: int = 0) -> None:
+    opts = GemmOptions(splits, cta_pair, B_LAYOUTS[b_layout], tile_n)
     check(load().trb_gemm_launch_ex(DTYPE_CODES[dtype], m, n, k, a, b, c, scale_a, scale_b, ctypes.byref(opts),
                                     stream or None))
 

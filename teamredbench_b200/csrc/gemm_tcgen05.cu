@@ -226,6 +226,7 @@ __device__ __forceinline__ int k_rotation(const SplitK& sk, int tile, int nk) {
     return sk.rotate_k && nk > 0 ? tile % nk : 0;
 }
 
+
 // KB: B is stored K-major (N x K row-major, "B transposed"); otherwise B is
 // the row-major K x N matrix, an MN-major operand.
 template <int DT, bool KB, int BN>
@@ -484,6 +485,300 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (first_epi_thread) sk.counters[tile] = 0u;  // ready for the next launch
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ swapped-operand skinny kernel
+// For M <= 64 a 128-row MMA tile is mostly padding, and its A boxes (128 rows
+// x 128 bytes per stage) crowd B out of shared memory.  This kernel computes
+// C^T = B^T * A^T instead: the MMA's M side (128 TMEM lanes) runs along N and
+// its N side (BS = 16, 32 or 64 columns) along the few rows of A.
+//  * wide operand W = B^T, 128 rows of N x one 128-byte K slice per stage:
+//    K-major when B is stored N x K, otherwise row-major B read in place
+//    through the MN-major swizzle (instruction-descriptor bit 15);
+//  * small operand S = A, BS rows x one 128-byte K slice, K-major (rows past
+//    M are zero-filled by TMA);
+//  * the ring is as deep as shared memory allows (11 stages at BS = 16), so
+//    each SM keeps ~176 KiB of B requests in flight, what streaming B at HBM
+//    rate needs;
+//  * work units are 128-column panels of C times K splits (the split count
+//    balances units over the SMs), with the main kernel's deterministic
+//    last-arrival split-K fix-up;
+//  * the epilogue thread of TMEM lane l owns column n = panel * 128 + l and
+//    writes its BS values down that column; for each row m the 32 lanes of a
+//    warp store 32 consecutive elements.
+template <int BS>
+struct SwapCfg {
+    static_assert(BS == 16 || BS == 32 || BS == 64, "swap tile width");
+    static constexpr int kSStage = BS * kBKBytes;
+    static constexpr int kStageBytes = kAStage + kSStage;
+    static constexpr int kStages = (210 * 1024) / kStageBytes > 12 ? 12 : (210 * 1024) / kStageBytes;
+    static constexpr int kTmemCols = kNumAcc * BS < 32 ? 32 : kNumAcc * BS;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+};
+
+// One output element from a 32-bit accumulator word (same conversions as store_chunk).
+template <int DT>
+__device__ __forceinline__ void store_elem(void* C, size_t idx, uint32_t v, float out_scale) {
+    if constexpr (DT == TRB_BFLOAT16 || DT == TRB_FLOAT8_E4M3FN) {
+        float f = __uint_as_float(v);
+        if constexpr (DT == TRB_FLOAT8_E4M3FN) f *= out_scale;
+        static_cast<__nv_bfloat16*>(C)[idx] = __float2bfloat16_rn(f);
+    } else if constexpr (DT == TRB_FLOAT16) {
+        static_cast<__half*>(C)[idx] = __float2half_rn(__uint_as_float(v));
+    } else {
+        static_cast<uint32_t*>(C)[idx] = v;
+    }
+}
+
+template <int BS>
+__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, uint32_t (&r)[BS]) {
+    if constexpr (BS == 16) {
+        tmem_ld_32x32b_x16(taddr, r);
+    } else {
+#pragma unroll
+        for (int c = 0; c < BS / 32; ++c)
+            tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+    }
+    tmem_wait_ld();
+}
+
+template <int DT, bool KB, int BS>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_swap_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
+                     void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
+    using Tr = Traits<DT>;
+    using Cfg = SwapCfg<BS>;
+    constexpr int kBKElems = kBKBytes / Tr::kEsize;
+    constexpr int kBoxN = 128 / Tr::kEsize;   // N elements per MN-major W box (one swizzle row)
+    constexpr int kWBoxes = kBM / kBoxN;      // MN-major W boxes per stage
+    constexpr int kWBoxBytes = kBKElems * 128;
+    constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;
+    constexpr int kStagesT = Cfg::kStages;
+    constexpr int kSStage = Cfg::kSStage;
+    // A operand = W (MN-major unless B is stored K-major), B operand = S (K-major), N = BS.
+    constexpr uint32_t kIdescS = idesc_with_n(idesc_b_kmajor(Tr::kIdesc) | (KB ? 0u : (1u << 15)), BS);
+
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kStagesT];
+    __shared__ __align__(8) uint64_t empty_bar[kStagesT];
+    __shared__ __align__(8) uint64_t accf_bar[kNumAcc];
+    __shared__ __align__(8) uint64_t acce_bar[kNumAcc];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    __shared__ int last_split_flag;
+
+    const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    const uint32_t sW = smem_base;
+    const uint32_t sS = smem_base + kStagesT * kAStage;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = (N + kBM - 1) / kBM;
+    const int num_kb = (K + kBKElems - 1) / kBKElems;
+    const int num_units = num_tiles * sk.splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStagesT; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        for (int a = 0; a < kNumAcc; ++a) {
+            mbar_init(smem_u32(&accf_bar[a]), 1);
+            mbar_init(smem_u32(&acce_bar[a]), 4);
+        }
+        mbar_init(smem_u32(&drain_bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmS);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;
+            bool ok = true;
+            for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+                const int tile = unit / sk.splits;
+                const int kb0 = (unit % sk.splits) * sk.kb_per_split;
+                const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
+                const int rot = k_rotation(sk, tile, nk);
+                for (int i = 0; i < nk; ++i) {
+                    const int kb = kb0 + (i + rot < nk ? i + rot : i + rot - nk);
+                    if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrProducerWait);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = smem_u32(&full_bar[stage]);
+                    mbar_arrive_expect_tx(fb, kAStage + kSStage);
+                    if constexpr (KB) {
+                        tma_load_2d(sW + stage * kAStage, &tmW, fb, kb * kBKElems, tile * kBM);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < kWBoxes; ++j)
+                            tma_load_2d(sW + stage * kAStage + j * kWBoxBytes, &tmW, fb, tile * kBM + j * kBoxN,
+                                        kb * kBKElems);
+                    }
+                    tma_load_2d(sS + stage * kSStage, &tmS, fb, kb * kBKElems, 0);
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStagesT) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            for (int s = 0; s < kStagesT; ++s)
+                if (issued_mask & (1u << s))
+                    if (!mbar_wait(smem_u32(&full_bar[s]), (issued_phase >> s) & 1u, nullptr))
+                        atomicCAS(&g_gemm_error, 0, kErrDrainWait);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer
+            const uint64_t a_desc0 = KB ? make_sdesc(sW, 16, 1024)
+                                        : make_sdesc(sW, kWBoxBytes, Tr::BLayout::kSbo, Tr::BLayout::kLayoutType);
+            const uint64_t b_desc0 = make_sdesc(sS, 16, 1024);
+            constexpr int kWStep = KB ? kInstrKBytes : kInstrKRows * 128;  // W bytes per instruction K step
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            int t_local = 0;
+            for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++t_local) {
+                const int kb0 = (unit % sk.splits) * sk.kb_per_split;
+                const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
+                const int acc = t_local & 1;
+                const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
+                if (!mbar_wait(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
+                    atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                    abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BS);
+                for (int i = 0; i < nk; ++i) {
+                    if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kAStage) >> 4);
+                    const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kSStage) >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < kKSteps; ++ks)
+                        mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kWStep >> 4),
+                                       b_stage + (uint64_t)(ks * kInstrKBytes >> 4), kIdescS,
+                                       (i != 0 || ks != 0) ? 1u : 0u);
+                    tc_commit(smem_u32(&empty_bar[stage]));
+                    if (++stage == kStagesT) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok) tc_commit(smem_u32(&accf_bar[acc]));
+            }
+            tc_commit(smem_u32(&drain_bar));
+            if (!mbar_wait(smem_u32(&drain_bar), 0, nullptr)) atomicCAS(&g_gemm_error, 0, kErrDrainWait);
+        }
+    } else {
+        // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+        const int q = warp & 3;
+        const int n_in_tile = q * 32 + lane;
+        const bool first_epi_thread = threadIdx.x == 64;
+        const int rows = M < BS ? M : BS;
+        int t_local = 0;
+        for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++t_local) {
+            const int tile = unit / sk.splits;
+            const int acc = t_local & 1;
+            const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
+            bool ok = mbar_wait(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
+            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int gn = tile * kBM + n_in_tile;
+            uint32_t r[BS];
+            tmem_ld_row<BS>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BS), r);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));  // TMEM free for the next unit
+            if (sk.splits == 1) {
+                if (gn < N) {
+#pragma unroll
+                    for (int m = 0; m < BS; ++m)
+                        if (m < rows) store_elem<DT>(C, (size_t)m * N + gn, r[m], out_scale);
+                }
+                continue;
+            }
+            // ---- split-K: publish this unit's fp32 partial (one TMEM lane = BS words)
+            {
+                uint4* w4 = reinterpret_cast<uint4*>(sk.ws + ((size_t)unit * kBM + n_in_tile) * BS);
+#pragma unroll
+                for (int i = 0; i < BS / 4; ++i) w4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+            }
+            __threadfence();
+            named_barrier(1, 128);
+            if (first_epi_thread)
+                last_split_flag = atomicAdd(&sk.counters[tile], 1u) == (unsigned)(sk.splits - 1);
+            named_barrier(1, 128);
+            if (!last_split_flag) continue;
+            __threadfence();
+            if (gn < N) {
+                const float* base = sk.ws + ((size_t)tile * sk.splits * kBM + n_in_tile) * BS;
+                float acc_f[BS];
+                const float4* p0 = reinterpret_cast<const float4*>(base);
+#pragma unroll
+                for (int i = 0; i < BS / 4; ++i) {
+                    const float4 v = __ldcg(p0 + i);
+                    acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
+                }
+                for (int sp = 1; sp < sk.splits; ++sp) {
+                    const float4* ps = reinterpret_cast<const float4*>(base + (size_t)sp * kBM * BS);
+#pragma unroll
+                    for (int i = 0; i < BS / 4; ++i) {
+                        const float4 v = __ldcg(ps + i);
+                        if constexpr (DT == TRB_INT8) {
+                            acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
+                            acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
+                            acc_f[4 * i + 2] = __int_as_float(__float_as_int(acc_f[4 * i + 2]) + __float_as_int(v.z));
+                            acc_f[4 * i + 3] = __int_as_float(__float_as_int(acc_f[4 * i + 3]) + __float_as_int(v.w));
+                        } else {
+                            acc_f[4 * i] += v.x; acc_f[4 * i + 1] += v.y; acc_f[4 * i + 2] += v.z; acc_f[4 * i + 3] += v.w;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < BS; ++m)
+                    if (m < rows) store_elem<DT>(C, (size_t)m * N + gn, __float_as_uint(acc_f[m]), out_scale);
+            }
+            if (first_epi_thread) sk.counters[tile] = 0u;
         }
     }
 
@@ -922,20 +1217,108 @@ static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, 
     return TRB_OK;
 }
 
+// Split count for the swapped kernel: minimise waves x k-blocks per unit
+// (+2 k-blocks of per-unit overhead: pipeline fill and epilogue), keeping
+// >= 4 k-blocks per split.  Ties keep the smaller split count.
+static int choose_swap_splits(long tiles, int num_kb, int sms) {
+    int best = 1;
+    long best_cost = -1;
+    const int max_s = std::max(1, std::min(32, num_kb / 4));
+    for (int s = 1; s <= max_s; ++s) {
+        const int kbps = (num_kb + s - 1) / s;
+        const int s_eff = (num_kb + kbps - 1) / kbps;
+        const long waves = (tiles * s_eff + sms - 1) / sms;
+        const long cost = waves * (kbps + 2);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = s_eff;
+        }
+    }
+    return best;
+}
+
+template <int DT, bool KB, int BS>
+static int launch_swap(const void* a, const void* b, int m, int n, int k, void* c, float out_scale, int splits,
+                       int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
+    using Tr = Traits<DT>;
+    using Cfg = SwapCfg<BS>;
+    constexpr int es = Tr::kEsize;
+    CUtensorMap tmW, tmS;
+    int rc = KB ? encode_2d(&tmW, b, es, (uint64_t)k, (uint64_t)n, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B)
+                : encode_2d(&tmW, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
+    if (rc != TRB_OK) return rc;
+    rc = encode_2d(&tmS, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, BS, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TRB_OK) return rc;
+    static bool attr_set[64] = {};
+    if (dev < 64 && !attr_set[dev]) {
+        TRB_CUDA(cudaFuncSetAttribute(gemm_swap_kernel<DT, KB, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)Cfg::kSmem));
+        attr_set[dev] = true;
+    }
+    const long tiles = (n + kBM - 1) / kBM;
+    const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
+    if (splits <= 0) splits = choose_swap_splits(tiles, num_kb, sms);
+    splits = std::max(1, std::min(splits, num_kb));
+    const int kbps = (num_kb + splits - 1) / splits;
+    splits = (num_kb + kbps - 1) / kbps;
+    // No K rotation: the A box is only BS x 128 bytes, and CTAs that walk K in
+    // step read whole rows of B together (measured 29.1 vs 30.7 us at
+    // M = 16, N = K = 8192 bf16 with per-tile rotation).
+    SplitK sk{splits, kbps, nullptr, nullptr, 0};
+    if (splits > 1) {
+        rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * BS * sizeof(float), (size_t)tiles, &sk);
+        if (rc != TRB_OK) return rc;
+    }
+    const long units = tiles * splits;
+    const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
+    gemm_swap_kernel<DT, KB, BS><<<grid, kThreads, Cfg::kSmem, stream>>>(tmW, tmS, c, m, n, k, out_scale, sk);
+    TRB_CUDA(cudaGetLastError());
+    if (info) {
+        *info = LaunchInfo{};
+        info->grid = grid;
+        info->block = kThreads;
+        info->splits = splits;
+        info->tile_n = BS;
+        info->swap = 1;
+    }
+    return TRB_OK;
+}
+
 template <int DT, bool KB>
 static int launch_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale, int splits,
-                        int cta_pair, cudaStream_t stream, LaunchInfo* info) {
+                        int cta_pair, int tile_n_opt, cudaStream_t stream, LaunchInfo* info) {
     using Tr = Traits<DT>;
     constexpr int es = Tr::kEsize;
     int dev = 0;
     TRB_CUDA(cudaGetDevice(&dev));
     const int sms = device_sm_count(dev);
+    // M <= 64: swapped operands (C^T = B^T A^T), unless a kernel is forced.
+    if (tile_n_opt < 0 || (tile_n_opt == 0 && cta_pair < 0 && m <= 64)) {
+        if (m > 64) {
+            set_error("trb_gemm_launch: the swapped-operand kernel takes m <= 64 (got %d)", m);
+            return TRB_ERR_ARGS;
+        }
+        if (m <= 16) return launch_swap<DT, KB, 16>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        if (m <= 32) return launch_swap<DT, KB, 32>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        return launch_swap<DT, KB, 64>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+    }
     // Automatic choice, from sustained clock-normalised measurements on B200
     // (8192^3, TFLOP/s per SM-GHz): the CTA pair (bf16 96%, e4m3 90% of the
     // per-clock tensor peak, vs 83% / 79% for one CTA), except for skinny
     // problems, which take narrow single-CTA tiles.
-    const int tile_n_single = choose_tile_n(m, n, es, KB, sms);
-    const bool pair = (cta_pair > 0 || (cta_pair < 0 && tile_n_single == 256)) && sms >= 2;
+    int tile_n_single = choose_tile_n(m, n, es, KB, sms);
+    if (tile_n_opt > 0) {
+        if (tile_n_opt != 64 && tile_n_opt != 128 && tile_n_opt != 256) {
+            set_error("trb_gemm_launch: tile_n must be 64, 128 or 256 (got %d)", tile_n_opt);
+            return TRB_ERR_ARGS;
+        }
+        if (tile_n_opt == 64 && es == 1 && !KB) {
+            set_error("trb_gemm_launch: 8-bit row-major B needs tile_n >= 128");
+            return TRB_ERR_ARGS;
+        }
+        tile_n_single = tile_n_opt;
+    }
+    const bool pair = (cta_pair > 0 || (cta_pair < 0 && tile_n_opt == 0 && tile_n_single == 256)) && sms >= 2;
     const int tile_n = pair ? kPairN : tile_n_single;
 
     CUtensorMap tmA, tmB;
@@ -1030,7 +1413,7 @@ struct Fp32x3Workspace {
 static Fp32x3Workspace g_fp32x3[64];
 
 static int launch_fp32x3(int m, int n, int k, const void* a, const void* b, void* c, int splits, int cta_pair,
-                         int b_kmajor, cudaStream_t stream, LaunchInfo* info) {
+                         int tile_n, int b_kmajor, cudaStream_t stream, LaunchInfo* info) {
     int dev = 0;
     TRB_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) {
@@ -1061,15 +1444,15 @@ static int launch_fp32x3(int m, int n, int k, const void* a, const void* b, void
         split3_tf32_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4*>(b), reinterpret_cast<float4*>(bp),
                                                      (uint64_t)k, (uint64_t)n / 4, kHiLoHi, 1);
     TRB_CUDA(cudaGetLastError());
-    const int rc = b_kmajor ? launch_typed<TRB_TFLOAT32, true>(m, n, 3 * k, ap, bp, c, 1.0f, splits, cta_pair, stream, info)
-                            : launch_typed<TRB_TFLOAT32, false>(m, n, 3 * k, ap, bp, c, 1.0f, splits, cta_pair, stream,
+    const int rc = b_kmajor ? launch_typed<TRB_TFLOAT32, true>(m, n, 3 * k, ap, bp, c, 1.0f, splits, cta_pair, tile_n, stream, info)
+                            : launch_typed<TRB_TFLOAT32, false>(m, n, 3 * k, ap, bp, c, 1.0f, splits, cta_pair, tile_n, stream,
                                                                 info);
     if (info) info->fp32x3 = 1;
     return rc;
 }
 
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
-           int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info) {
+           int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info, int tile_n) {
     if (m <= 0 || n <= 0 || k <= 0 || a == nullptr || b == nullptr || c == nullptr) {
         set_error("trb_gemm_launch: dimensions must be positive and pointers non-null");
         return TRB_ERR_ARGS;
@@ -1094,26 +1477,26 @@ int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c
         set_error("trb_gemm_launch: splits must be >= 0");
         return TRB_ERR_ARGS;
     }
-    if (dtype == TRB_FLOAT32) return launch_fp32x3(m, n, k, a, b, c, splits, cta_pair, b_kmajor, stream, info);
+    if (dtype == TRB_FLOAT32) return launch_fp32x3(m, n, k, a, b, c, splits, cta_pair, tile_n, b_kmajor, stream, info);
     if (b_kmajor) {
         switch (dtype) {
-            case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
-            case TRB_FLOAT16: return launch_typed<TRB_FLOAT16, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
-            case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
+            case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
+            case TRB_FLOAT16: return launch_typed<TRB_FLOAT16, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
+            case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
             case TRB_FLOAT8_E4M3FN:
                 return launch_typed<TRB_FLOAT8_E4M3FN, true>(m, n, k, a, b, c, scale_a * scale_b, splits, cta_pair,
-                                                             stream, info);
-            default: return launch_typed<TRB_INT8, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
+                                                             tile_n, stream, info);
+            default: return launch_typed<TRB_INT8, true>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
         }
     }
     switch (dtype) {
-        case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
-        case TRB_FLOAT16: return launch_typed<TRB_FLOAT16, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
-        case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
+        case TRB_BFLOAT16: return launch_typed<TRB_BFLOAT16, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
+        case TRB_FLOAT16: return launch_typed<TRB_FLOAT16, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
+        case TRB_TFLOAT32: return launch_typed<TRB_TFLOAT32, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
         case TRB_FLOAT8_E4M3FN:
             return launch_typed<TRB_FLOAT8_E4M3FN, false>(m, n, k, a, b, c, scale_a * scale_b, splits, cta_pair,
-                                                          stream, info);
-        default: return launch_typed<TRB_INT8, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, stream, info);
+                                                          tile_n, stream, info);
+        default: return launch_typed<TRB_INT8, false>(m, n, k, a, b, c, 1.0f, splits, cta_pair, tile_n, stream, info);
     }
 }
 
@@ -1363,7 +1746,7 @@ extern "C" int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a,
         return TRB_ERR_ARGS;
     }
     return trb::gemm::launch(dtype, m, n, k, a, b, c, scale_a, scale_b, o.splits, o.cta_pair,
-                             o.b_layout == TRB_B_K_MAJOR, static_cast<cudaStream_t>(stream), nullptr);
+                             o.b_layout == TRB_B_K_MAJOR, static_cast<cudaStream_t>(stream), nullptr, o.tile_n);
 }
 
 extern "C" int trb_round_tf32(void* data, uint64_t count, void* stream) {

@@ -49,12 +49,15 @@ struct LaunchInfo {
     int grid = 0, block = 0, splits = 1, pair = 0, tile_n = 256;
     int fp32x3 = 0;   // float32 computed as three tf32 products
     int fp64 = 0;     // float64 CUDA-core kernel
+    int swap = 0;     // swapped-operand skinny kernel (C^T = B^T A^T); tile_n = its MMA N
 };
 // splits: 0 = automatic (split-K only for problems that leave SMs idle), >= 1 forced.
 // cta_pair: < 0 automatic (pair, or narrow single-CTA tiles when skinny), 0 single-CTA, > 0 CTA pair.
 // b_kmajor: B is stored N x K (K-major) instead of the row-major K x N matrix.
+// tile_n: 0 automatic; 64 / 128 / 256 force the single-CTA kernel at that tile
+// width; < 0 forces the swapped-operand kernel (m <= 64).
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
-           int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info);
+           int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info, int tile_n = 0);
 int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsigned int* absmax_scratch,
                  float* scale_out, cudaStream_t stream);
 int read_error(bool clear);
@@ -332,6 +335,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+// 32 lanes x 16 consecutive 32-bit TMEM columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

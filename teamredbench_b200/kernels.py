@@ -64,7 +64,8 @@ def stream_op(mode: str, dst: Any, src: Any, aux: Any | None = None, scale: floa
 
 
 def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float = 1.0, scale_b: float = 1.0,
-         splits: int = 0, cta_pair: int = -1, b_transposed: bool = False, stream: Any | None = None) -> Any:
+         splits: int = 0, cta_pair: int = -1, b_transposed: bool = False, stream: Any | None = None,
+         tile_n: int = 0) -> Any:
     """out = a @ b on the tcgen05 kernel; a (m x k) and b (k x n) row-major.
     With b_transposed=True, `b` holds B^T as a row-major (n x k) tensor.
 
@@ -74,7 +75,10 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     e4m3 inputs, f16 for f16, f32 for tf32 and float32, f64 for float64, int32
     for int8.
     splits: 0 = automatic split-K, >= 1 forces that many K splits.
-    cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel."""
+    cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel.
+    tile_n: 0 automatic, 64/128/256 single-CTA tile width, < 0 the
+    swapped-operand skinny kernel (C^T = B^T A^T, m <= 64; automatic for
+    m <= 64)."""
     _require_cuda_contiguous(a, b, out)
     bk, bn = (b.shape[1], b.shape[0]) if b_transposed else (b.shape[0], b.shape[1])
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != bk:
@@ -86,5 +90,5 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     name = dtype or trb_dtype(a)
     _native.gemm_launch_ex(name, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), float(scale_a),
                            float(scale_b), int(splits), int(cta_pair), "k_major" if b_transposed else "row_major",
-                           _stream_handle(a, stream))
+                           _stream_handle(a, stream), int(tile_n))
     return out

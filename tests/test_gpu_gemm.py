@@ -145,10 +145,12 @@ def test_pair_and_single_agree_bitwise_for_int8():
 
 
 def test_split_k_run_entry_reports_splits():
-    res = _native.gemm_run("bfloat16", 16, 1024, 8192, 1, 3)  # 16 narrow tiles: K is split too
-    assert res.split_k > 1 and res.device_error == 0
-    assert res.implementation.decode() == "tcgen05_1cta_128x64_splitk"
-    res = _native.gemm_run("bfloat16", 16, 8192, 8192, 1, 3)  # 128 narrow tiles: no split needed
+    res = _native.gemm_run("bfloat16", 16, 1024, 8192, 1, 3)  # 8 swapped panels: K is split 16 ways
+    assert res.split_k == 16 and res.device_error == 0
+    assert res.implementation.decode() == "tcgen05_swap_128x16_splitk"
+    res = _native.gemm_run("bfloat16", 16, 8192, 8192, 1, 3)  # 64 panels x 2 splits
+    assert res.split_k == 2 and res.implementation.decode() == "tcgen05_swap_128x16_splitk"
+    res = _native.gemm_run("bfloat16", 128, 8192, 8192, 1, 3)  # 128 narrow tiles: no split needed
     assert res.split_k == 1 and res.implementation.decode() == "tcgen05_1cta_128x64"
     res = _native.gemm_run("bfloat16", 4096, 4096, 4096, 1, 3)
     assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x256"
@@ -316,3 +318,56 @@ def test_high_precision_host_entry(name):
     res = _native.gemm_host(name, m, n, k, ha.data_ptr(), hb.data_ptr(), hc.data_ptr())
     assert res.device_error == 0
     _check(name, a, b, hc, 1.0, 1.0, np.arange(m))
+
+
+# ---------------------------------------------------------------------------
+# Swapped-operand skinny kernel (M <= 64): C^T = B^T A^T with the rows of A as
+# the MMA's N (16 / 32 / 64).
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name", DTYPES)
+@pytest.mark.parametrize("shape", [(1, 256, 512), (16, 8192, 8192), (17, 640, 1024), (32, 4096, 2048),
+                                   (48, 1040, 4096), (64, 2048, 8192), (5, 144, 96)])
+@pytest.mark.parametrize("b_transposed", [False, True])
+@pytest.mark.parametrize("splits", [0, 1, 5])
+def test_swap_kernel(name, shape, b_transposed, splits):
+    m, n, k = shape
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=3 * m + n + k)
+    bb = b.t().contiguous() if b_transposed else b
+    out = lambda: torch.empty((m, n), device="cuda", dtype=torch_dtype(GEMM_OUT[name]))  # noqa: E731
+    c1, c2 = out(), out()
+    for c in (c1, c2):
+        gemm(a, bb, c, dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, splits=splits, tile_n=-1)
+    torch.cuda.synchronize()
+    assert torch.equal(c1, c2)  # deterministic, split-K included
+    num_kb = -(-k * b.element_size() // 128)
+    per_split = k if splits <= 1 else k * -(-num_kb // splits) // num_kb
+    _check(name, a, b, c1, sa, sb, np.arange(m), tol=gemm_tolerance(name, per_split))
+
+
+@pytest.mark.parametrize("b_transposed", [False, True])
+def test_swap_and_tile_kernels_agree_bitwise_for_int8(b_transposed):
+    a, b, _, _ = gemm_operands("int8", 40, 2048, 4096, seed=2)
+    bb = b.t().contiguous() if b_transposed else b
+    outs = []
+    for kw in ({"tile_n": -1}, {"tile_n": 128}, {"cta_pair": 1}):
+        c = torch.empty((40, 2048), device="cuda", dtype=torch.int32)
+        gemm(a, bb, c, b_transposed=b_transposed, **kw)
+        outs.append(c)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
+def test_swap_kernel_is_automatic_for_m_le_64_and_validates_options():
+    a, b, _, _ = gemm_operands("bfloat16", 65, 512, 256, seed=1)
+    c = torch.empty((65, 512), device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(_native.NativeError):
+        gemm(a, b, c, tile_n=-1)  # the swapped kernel takes m <= 64
+    with pytest.raises(_native.NativeError):
+        gemm(a, b, c, tile_n=96)
+    gemm(a, b, c, tile_n=64)
+    torch.cuda.synchronize()
+    _check("bfloat16", a, b, c, 1.0, 1.0, np.arange(65))
+    res = _native.gemm_run("float8_e4m3fn", 64, 4096, 4096, 1, 2)
+    assert res.implementation.decode().startswith("tcgen05_swap_128x64") and res.device_error == 0
+    res = _native.gemm_run("float32", 32, 4096, 4096, 1, 2)
+    assert res.implementation.decode().startswith("fp32x3_tcgen05_swap_128x32") and res.device_error == 0
