@@ -119,7 +119,8 @@ typedef struct trb_gemm_args {
 
 /* Kernel choices for trb_gemm_launch_ex. */
 typedef struct trb_gemm_options {
-    int32_t splits;          /* 0 = automatic split-K; >= 1 forces that many K splits */
+    int32_t splits;          /* 0 = automatic split-K; >= 1 forces that many K splits (global workspace);
+                                -2 / -4 / -8 = that many splits reduced inside a thread-block cluster */
     int32_t cta_pair;        /* < 0 automatic, 0 = single-CTA 128 x 256 tiles, > 0 = CTA-pair 256 x 256 tiles */
     int32_t b_layout;        /* trb_b_layout */
     int32_t tile_n;          /* 0 = automatic; 64, 128 or 256 = single-CTA kernel with tiles of that width;
@@ -211,6 +212,13 @@ int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b
  *            tile width (8-bit row-major B: >= 128); < 0 forces the
  *            swapped-operand kernel (m <= 64).  Explicit cta_pair >= 0 also
  *            turns the automatic swapped choice off.
+ *  splits < 0: cluster split-K -- the K splits of a tile run as one
+ *            thread-block cluster (2, 4 or 8 CTAs, one tile each, every split
+ *            owning >= 1 k-block) and are reduced through distributed shared
+ *            memory in split order (bit-identical to the workspace split-K
+ *            with the same count).  Swapped-operand or 128 x 256 single-CTA
+ *            kernel.  Automatic for skinny problems whose tiles leave more
+ *            than half of the SMs idle.
  * No reference counterpart: the reference's native GEMM has one tile shape
  * and no split-K (mfu_gemm_lowp.hip.hpp:423-431). */
 int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void* b, void* c,

@@ -229,7 +229,15 @@ __device__ __forceinline__ int k_rotation(const SplitK& sk, int tile, int nk) {
 
 // KB: B is stored K-major (N x K row-major, "B transposed"); otherwise B is
 // the row-major K x N matrix, an MN-major operand.
-template <int DT, bool KB, int BN>
+// CL > 1: cluster split-K for skinny problems.  The grid is tiles x CL, one
+// unit per CTA, the CL CTAs of a cluster are the K splits of one tile (rank =
+// split).  After every CTA's main loop has drained, the shared-memory rings
+// are free: rank r owns columns [r * BN / CL, (r + 1) * BN / CL) of the tile,
+// every CTA writes its fp32 partials of each column block into the owner's
+// ring (distributed shared memory), and the owner sums the CL partials in
+// split order -- the order, hence the bits, of the workspace fix-up -- and
+// stores C.  No workspace and no L2 round trips after the main loop.
+template <int DT, bool KB, int BN, int CL = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
@@ -244,6 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kBStageT = Cfg::kBStage;
     constexpr uint32_t kIdesc1 = idesc_with_n(KB ? idesc_b_kmajor(Tr::kIdesc) : Tr::kIdesc, BN);
     static_assert(KB || BN >= kBoxN, "MN-major B needs at least one 128-byte swizzle row per tile");
+    static_assert(CL == 1 || ((CL == 2 || CL == 4 || CL == 8) && (BN / CL) % 32 == 0), "cluster split");
+    static_assert(CL == 1 || (size_t)kBM * BN * 4 <= (size_t)kStagesT * (kAStage + kBStageT), "receive buffer");
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kStagesT];
@@ -254,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     __shared__ int last_split_flag;
+    __shared__ __align__(8) uint64_t recv_bar;  // cluster split-K: the peers' partials have landed
 
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = smem_base;
@@ -277,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&acce_bar[a]), 4);  // one arrival per epilogue warp
         }
         mbar_init(smem_u32(&drain_bar), 1);
+        if constexpr (CL > 1) mbar_init(smem_u32(&recv_bar), 1);
         abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -290,10 +302,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_slot;
+    // The next grid may set up (barriers, TMEM, descriptors) while this one
+    // runs; it reads and writes global memory only after its own wait.
+    grid_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer
+            grid_dependency_wait();  // A and B may be outputs of the previous grid
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;  // per stage: a load is outstanding / its parity
             bool ok = true;
@@ -387,8 +403,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_commit(smem_u32(&drain_bar));
             if (!mbar_wait(smem_u32(&drain_bar), 0, nullptr)) atomicCAS(&g_gemm_error, 0, kErrDrainWait);
         }
-    } else {
+    } else if constexpr (CL == 1) {
         // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+        grid_dependency_wait();  // C and the split-K workspace may be in use by the previous grid
         const int q = warp & 3;
         const int row_in_tile = q * 32 + lane;
         const bool first_epi_thread = threadIdx.x == 64;
@@ -488,6 +505,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if constexpr (CL > 1) {
+        // ---------------- cluster split-K epilogue (one unit per CTA)
+        const bool epi = warp >= 2;
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        bool ok = true;
+        if (epi) {
+            grid_dependency_wait();
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf_bar[0]), 0, &abort_flag));
+            if (!ok && lane == 0) {
+                atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+                abort_flag = 1;
+            }
+            tc_fence_after();
+        }
+        __syncwarp();
+        cluster_sync_all();  // every CTA's MMAs and TMA writes are done: the rings can receive
+        constexpr int kOwnCols = BN / CL;
+        constexpr int kOwnChunks = kOwnCols / 32;
+        const int rank = (int)cluster_ctarank();
+        // Receive buffer in the ring: 16-byte slots [src rank][owned 32-column
+        // chunk][float4 i][row], row-minor, so the 32 lanes of one store (or
+        // load) cover 512 contiguous bytes.  Peers' slots arrive by st.async,
+        // completing on recv_bar; this CTA's own slots are written and read
+        // back by the same thread.
+        const uint32_t sRecv = smem_base;
+        const uint32_t recv_bar_addr = smem_u32(&recv_bar);
+        if (epi && ok) {
+            if (threadIdx.x == 64) mbar_arrive_expect_tx(recv_bar_addr, (uint32_t)((CL - 1) * kOwnCols * kBM * 4));
+            uint4* recv4 = reinterpret_cast<uint4*>(smem_raw + (sRecv - smem_u32(smem_raw)));
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+                tmem_wait_ld();
+                const int owner = c / kOwnChunks;
+                const int slot0 = ((rank * kOwnChunks + c % kOwnChunks) * 8) * kBM + row_in_tile;
+                if (owner == rank) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        recv4[slot0 + i * kBM] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+                } else {
+                    const uint32_t dst = mapa_shared(sRecv + (uint32_t)(slot0 * 16), (uint32_t)owner);
+                    const uint32_t bar = mapa_shared(recv_bar_addr, (uint32_t)owner);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        st_async_v4(dst + (uint32_t)(i * kBM * 16),
+                                    make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]), bar);
+                }
+            }
+            if (!mbar_wait_cluster(recv_bar_addr, 0, &abort_flag)) {
+                atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+                abort_flag = 1;
+                ok = false;
+            }
+        }
+        if (epi && ok) {
+            int mb, nb;
+            tile_coords((int)blockIdx.x / CL, num_m, num_n, mb, nb);
+            const int grow = mb * kBM + row_in_tile;
+            const float4* recv = reinterpret_cast<const float4*>(smem_raw + (sRecv - smem_u32(smem_raw)));
+            if (grow < M) {
+#pragma unroll 1
+                for (int cc = 0; cc < kOwnChunks; ++cc) {
+                    const int gcol = nb * BN + rank * kOwnCols + cc * 32;
+                    if (gcol >= N) break;
+                    float acc_f[32];
+#pragma unroll
+                    for (int src = 0; src < CL; ++src) {  // split order
+                        const float4* p4 = recv + (size_t)(src * kOwnChunks + cc) * 8 * kBM + row_in_tile;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 v = p4[i * kBM];
+                            if (src == 0) {
+                                acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
+                            } else if constexpr (DT == TRB_INT8) {
+                                acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
+                                acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
+                                acc_f[4 * i + 2] = __int_as_float(__float_as_int(acc_f[4 * i + 2]) + __float_as_int(v.z));
+                                acc_f[4 * i + 3] = __int_as_float(__float_as_int(acc_f[4 * i + 3]) + __float_as_int(v.w));
+                            } else {
+                                acc_f[4 * i] += v.x; acc_f[4 * i + 1] += v.y; acc_f[4 * i + 2] += v.z; acc_f[4 * i + 3] += v.w;
+                            }
+                        }
+                    }
+                    uint32_t r[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(acc_f[i]);
+                    store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+                }
+            }
+        }
+        __syncwarp();
+        cluster_sync_all();  // no CTA leaves while a peer's stores may still target it
+    }
+
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -515,14 +629,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 //  * the epilogue thread of TMEM lane l owns column n = panel * 128 + l and
 //    writes its BS values down that column; for each row m the 32 lanes of a
 //    warp store 32 consecutive elements.
-template <int BS>
+template <int BS, int KD, int CL>
 struct SwapCfg {
     static_assert(BS == 16 || BS == 32 || BS == 64, "swap tile width");
-    static constexpr int kSStage = BS * kBKBytes;
-    static constexpr int kStageBytes = kAStage + kSStage;
-    static constexpr int kStages = (210 * 1024) / kStageBytes > 12 ? 12 : (210 * 1024) / kStageBytes;
+    static_assert(KD == 1 || KD == 2 || KD == 4, "k-blocks per stage");
+    static_assert(CL == 1 || CL == 2 || CL == 4 || CL == 8, "cluster split count");
+    static constexpr int kSBlock = BS * kBKBytes;          // one k-block of S
+    static constexpr int kWStage = KD * kAStage;            // KD k-blocks of W (128 rows each)
+    static constexpr int kSStage = KD * kSBlock;
+    static constexpr int kStageBytes = kWStage + kSStage;
+    // Cluster split-K: fp32 partials of the lanes this CTA owns, one slot per peer.
+    static constexpr int kRecvBytes = CL > 1 ? kBM * BS * 4 : 0;
+    static constexpr int kRingBudget = 210 * 1024 - kRecvBytes;
+    static constexpr int kStages = kRingBudget / kStageBytes > 12 ? 12 : kRingBudget / kStageBytes;
+    static_assert(kStages >= 2, "ring too shallow");
     static constexpr int kTmemCols = kNumAcc * BS < 32 ? 32 : kNumAcc * BS;
-    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + kRecvBytes + 1024;
 };
 
 // One output element from a 32-bit accumulator word (same conversions as store_chunk).
@@ -551,21 +673,33 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, uint32_t (&r)[BS]) {
     tmem_wait_ld();
 }
 
-template <int DT, bool KB, int BS>
+// CL > 1: cluster split-K.  The grid is tiles x CL, one unit per CTA, and the
+// CL CTAs of a cluster are the K splits of one tile (cluster rank = split).
+// Rank r owns TMEM lanes [r * 128 / CL, (r + 1) * 128 / CL): every CTA writes
+// the partials of lanes it does not own into the owner's receive buffer
+// (distributed shared memory), then arrives on the owner's receive barrier;
+// the owner sums the CL partials in split order -- the same order, hence the
+// same bits, as the global-workspace fix-up -- and stores C.  No workspace,
+// no counters, and no round trips through L2 after the main loop.
+template <int DT, bool KB, int BS, int KD, int CL>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_swap_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                      void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
     using Tr = Traits<DT>;
-    using Cfg = SwapCfg<BS>;
+    using Cfg = SwapCfg<BS, KD, CL>;
     constexpr int kBKElems = kBKBytes / Tr::kEsize;
     constexpr int kBoxN = 128 / Tr::kEsize;   // N elements per MN-major W box (one swizzle row)
     constexpr int kWBoxes = kBM / kBoxN;      // MN-major W boxes per stage
-    constexpr int kWBoxBytes = kBKElems * 128;
+    constexpr int kWBoxBytes = KD * kBKElems * 128;  // one MN-major W box: KD k-blocks tall
+    constexpr int kWKBlockBytes = kBKElems * 128;    // one k-block inside such a box
     constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;
     constexpr int kStagesT = Cfg::kStages;
+    constexpr int kWStage = Cfg::kWStage;
     constexpr int kSStage = Cfg::kSStage;
+    constexpr int kSBlock = Cfg::kSBlock;
     // A operand = W (MN-major unless B is stored K-major), B operand = S (K-major), N = BS.
     constexpr uint32_t kIdescS = idesc_with_n(idesc_b_kmajor(Tr::kIdesc) | (KB ? 0u : (1u << 15)), BS);
+    static_assert(KB || KD * kBKElems <= 256, "TMA box height");
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kStagesT];
@@ -576,10 +710,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     __shared__ int last_split_flag;
+    __shared__ __align__(8) uint64_t recv_bar;  // cluster split-K: the peers' partials have landed
 
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sW = smem_base;
-    const uint32_t sS = smem_base + kStagesT * kAStage;
+    const uint32_t sS = smem_base + kStagesT * kWStage;
+    const uint32_t sRecv = sS + kStagesT * kSStage;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -597,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&acce_bar[a]), 4);
         }
         mbar_init(smem_u32(&drain_bar), 1);
+        if constexpr (CL > 1) mbar_init(smem_u32(&recv_bar), 1);
         abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmW);
@@ -610,10 +747,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_slot;
+    if constexpr (CL > 1) cluster_sync_all();  // peers' receive barriers initialised before any arrival
+    // The next grid may set up (barriers, TMEM, descriptors) while this one
+    // streams; it reads and writes global memory only after its own wait.
+    grid_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer
+            grid_dependency_wait();  // A and B may be outputs of the previous grid
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;
             bool ok = true;
@@ -621,9 +763,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int tile = unit / sk.splits;
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
                 const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
-                const int rot = k_rotation(sk, tile, nk);
-                for (int i = 0; i < nk; ++i) {
-                    const int kb = kb0 + (i + rot < nk ? i + rot : i + rot - nk);
+                for (int g = 0; g * KD < nk; ++g) {  // one stage = KD consecutive k-blocks
+                    const int kbg = kb0 + g * KD;
+                    const int valid = min(KD, nk - g * KD);
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrProducerWait);
                         abort_flag = 1;
@@ -631,16 +773,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
-                    mbar_arrive_expect_tx(fb, kAStage + kSStage);
+                    // MN-major W boxes always span KD k-blocks (rows past K are
+                    // zero-filled, rows of the next split are loaded but unused).
+                    mbar_arrive_expect_tx(fb, (uint32_t)((KB ? valid * kAStage : kWStage) + valid * kSBlock));
                     if constexpr (KB) {
-                        tma_load_2d(sW + stage * kAStage, &tmW, fb, kb * kBKElems, tile * kBM);
+                        for (int i = 0; i < valid; ++i)
+                            tma_load_2d(sW + stage * kWStage + i * kAStage, &tmW, fb, (kbg + i) * kBKElems, tile * kBM);
                     } else {
 #pragma unroll
                         for (int j = 0; j < kWBoxes; ++j)
-                            tma_load_2d(sW + stage * kAStage + j * kWBoxBytes, &tmW, fb, tile * kBM + j * kBoxN,
-                                        kb * kBKElems);
+                            tma_load_2d(sW + stage * kWStage + j * kWBoxBytes, &tmW, fb, tile * kBM + j * kBoxN,
+                                        kbg * kBKElems);
                     }
-                    tma_load_2d(sS + stage * kSStage, &tmS, fb, kb * kBKElems, 0);
+                    for (int i = 0; i < valid; ++i)
+                        tma_load_2d(sS + stage * kSStage + i * kSBlock, &tmS, fb, (kbg + i) * kBKElems, 0);
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == kStagesT) {
@@ -661,6 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         : make_sdesc(sW, kWBoxBytes, Tr::BLayout::kSbo, Tr::BLayout::kLayoutType);
             const uint64_t b_desc0 = make_sdesc(sS, 16, 1024);
             constexpr int kWStep = KB ? kInstrKBytes : kInstrKRows * 128;  // W bytes per instruction K step
+            constexpr int kWBlock = KB ? kAStage : kWKBlockBytes;          // W bytes per k-block in a stage
             uint32_t stage = 0, phase = 0;
             bool ok = true;
             int t_local = 0;
@@ -676,20 +823,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BS);
-                for (int i = 0; i < nk; ++i) {
+                for (int g = 0; g * KD < nk; ++g) {
+                    const int valid = min(KD, nk - g * KD);
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
                         ok = false;
                         break;
                     }
-                    const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kAStage) >> 4);
+                    const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kWStage) >> 4);
                     const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kSStage) >> 4);
+                    for (int i = 0; i < valid; ++i) {
 #pragma unroll
-                    for (int ks = 0; ks < kKSteps; ++ks)
-                        mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kWStep >> 4),
-                                       b_stage + (uint64_t)(ks * kInstrKBytes >> 4), kIdescS,
-                                       (i != 0 || ks != 0) ? 1u : 0u);
+                        for (int ks = 0; ks < kKSteps; ++ks)
+                            mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)((i * kWBlock + ks * kWStep) >> 4),
+                                           b_stage + (uint64_t)((i * kSBlock + ks * kInstrKBytes) >> 4), kIdescS,
+                                           (g != 0 || i != 0 || ks != 0) ? 1u : 0u);
+                    }
                     tc_commit(smem_u32(&empty_bar[stage]));
                     if (++stage == kStagesT) {
                         stage = 0;
@@ -703,6 +853,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- epilogue: warps 2..5 own TMEM lane quarters (warp % 4)
+        grid_dependency_wait();  // C and the split-K workspace may be in use by the previous grid
         const int q = warp & 3;
         const int n_in_tile = q * 32 + lane;
         const bool first_epi_thread = threadIdx.x == 64;
@@ -734,6 +885,62 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int m = 0; m < BS; ++m)
                         if (m < rows) store_elem<DT>(C, (size_t)m * N + gn, r[m], out_scale);
+                }
+                continue;
+            }
+            if constexpr (CL > 1) {
+                // ---- cluster split-K through distributed shared memory
+                constexpr int kOwn = kBM / CL;
+                const int rank = (int)cluster_ctarank();
+                const int owner = n_in_tile / kOwn;
+                const int slot = n_in_tile % kOwn;
+                // Receive buffer: 16-byte slots [src rank][float4 i][owned lane], lane-minor
+                // so one store (or load) of a warp covers 512 contiguous bytes.  Peers'
+                // partials arrive by st.async and complete on the owner's recv_bar.
+                if (owner != rank) {
+                    const uint32_t dst =
+                        mapa_shared(sRecv + (uint32_t)((rank * (BS / 4) * kOwn + slot) * 16), (uint32_t)owner);
+                    const uint32_t bar = mapa_shared(smem_u32(&recv_bar), (uint32_t)owner);
+#pragma unroll
+                    for (int i = 0; i < BS / 4; ++i)
+                        st_async_v4(dst + (uint32_t)(i * kOwn * 16),
+                                    make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]), bar);
+                }
+                if (first_epi_thread) mbar_arrive_expect_tx(smem_u32(&recv_bar), (uint32_t)((CL - 1) * kOwn * BS * 4));
+                if (owner == rank) {
+                    if (!mbar_wait_cluster(smem_u32(&recv_bar), 0, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+                        abort_flag = 1;
+                    } else if (gn < N) {
+                        const float* recv = reinterpret_cast<const float*>(smem_raw + (sRecv - smem_u32(smem_raw)));
+                        float acc_f[BS];
+#pragma unroll
+                        for (int src = 0; src < CL; ++src) {  // split order: src 0 first, as in the workspace fix-up
+#pragma unroll
+                            for (int i = 0; i < BS / 4; ++i) {
+                                float4 v;
+                                if (src == rank) {
+                                    v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                    __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                                } else {
+                                    v = reinterpret_cast<const float4*>(recv)[(size_t)(src * (BS / 4) + i) * kOwn + slot];
+                                }
+                                if (src == 0) {
+                                    acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
+                                } else if constexpr (DT == TRB_INT8) {
+                                    acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
+                                    acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
+                                    acc_f[4 * i + 2] = __int_as_float(__float_as_int(acc_f[4 * i + 2]) + __float_as_int(v.z));
+                                    acc_f[4 * i + 3] = __int_as_float(__float_as_int(acc_f[4 * i + 3]) + __float_as_int(v.w));
+                                } else {
+                                    acc_f[4 * i] += v.x; acc_f[4 * i + 1] += v.y; acc_f[4 * i + 2] += v.z; acc_f[4 * i + 3] += v.w;
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int m = 0; m < BS; ++m)
+                            if (m < rows) store_elem<DT>(C, (size_t)m * N + gn, __float_as_uint(acc_f[m]), out_scale);
+                    }
                 }
                 continue;
             }
@@ -784,6 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (CL > 1) cluster_sync_all();  // no CTA leaves while a peer may still write into it
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem_base, Cfg::kTmemCols);
@@ -884,10 +1092,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync_all();  // barrier inits of both CTAs visible before any cross-CTA signal
     tc_fence_after();
     const uint32_t tmem_base = tmem_slot;
+    grid_launch_dependents();  // the next grid may set up; its global accesses wait for this one
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer (both CTAs; completion on the leader's full barriers)
+            grid_dependency_wait();  // A and B may be outputs of the previous grid
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;
             bool ok = true;
@@ -979,6 +1189,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- epilogue (both CTAs): warps 2..5 read this CTA's 128 accumulator rows
+        grid_dependency_wait();  // C and the split-K workspace may be in use by the previous grid
         const int q = warp & 3;
         const int row_in_tile = q * 32 + lane;
         const bool first_epi_thread = threadIdx.x == 64;
@@ -1187,34 +1398,108 @@ static int choose_tile_n(int m, int n, int es, bool kb, int sms) {
     return (es >= 2 || kb) ? 64 : 128;
 }
 
-template <int DT, bool KB, int BN>
+// Launch with programmatic stream serialization (the kernels' griddepcontrol
+// waits order their global accesses after the previous grid) and, for
+// cluster split-K, the cluster shape.
+template <typename Kernel, typename... Args>
+static int launch_ex(Kernel kernel, int grid, size_t smem, int cluster, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    int nattr = 0;
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+    if (cluster > 1) {
+        attr[nattr].id = cudaLaunchAttributeClusterDimension;
+        attr[nattr].val.clusterDim.x = (unsigned)cluster;
+        attr[nattr].val.clusterDim.y = 1;
+        attr[nattr].val.clusterDim.z = 1;
+        ++nattr;
+    }
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = nattr;
+    TRB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
+    return TRB_OK;
+}
+
+template <int DT, bool KB, int BN, int CL = 1>
 static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, int n, int k, void* c,
                          float out_scale, int splits, int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
     using Tr = Traits<DT>;
     using Cfg = TileCfg<BN>;
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {
-        TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, KB, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, KB, BN, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)Cfg::kSmem));
         attr_set[dev] = true;
     }
     const long tiles = (long)((m + kBM - 1) / kBM) * ((n + BN - 1) / BN);
     const int num_kb = (int)(((long)k * Tr::kEsize + kBKBytes - 1) / kBKBytes);
-    if (splits <= 0) splits = choose_splits(tiles, num_kb, sms);
-    splits = std::max(1, std::min(splits, num_kb));
-    const int kbps = (num_kb + splits - 1) / splits;
-    splits = (num_kb + kbps - 1) / kbps;  // every split owns at least one k-block
-    SplitK sk{splits, kbps, nullptr, nullptr, m <= kBM ? 1 : 0};
-    if (splits > 1) {
-        const int rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * BN * sizeof(float), (size_t)tiles, &sk);
-        if (rc != TRB_OK) return rc;
+    SplitK sk{1, num_kb, nullptr, nullptr, m <= kBM ? 1 : 0};
+    int grid;
+    if constexpr (CL > 1) {
+        sk.splits = CL;
+        sk.kb_per_split = (num_kb + CL - 1) / CL;  // the caller checked that every split owns >= 1 k-block
+        grid = (int)(tiles * CL);
+    } else {
+        if (splits <= 0) splits = choose_splits(tiles, num_kb, sms);
+        splits = std::max(1, std::min(splits, num_kb));
+        const int kbps = (num_kb + splits - 1) / splits;
+        splits = (num_kb + kbps - 1) / kbps;  // every split owns at least one k-block
+        sk.splits = splits;
+        sk.kb_per_split = kbps;
+        if (splits > 1) {
+            const int rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * BN * sizeof(float), (size_t)tiles, &sk);
+            if (rc != TRB_OK) return rc;
+        }
+        grid = (int)std::max<long>(1, std::min<long>(tiles * splits, sms));
     }
-    const long units = tiles * splits;
-    const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
-    gemm_tcgen05_kernel<DT, KB, BN><<<grid, kThreads, Cfg::kSmem, stream>>>(tmA, tmB, c, m, n, k, out_scale, sk);
+    const int rc = launch_ex(gemm_tcgen05_kernel<DT, KB, BN, CL>, grid, Cfg::kSmem, CL, stream, tmA, tmB, c, m, n, k,
+                             out_scale, sk);
+    if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaGetLastError());
-    if (info) *info = {grid, kThreads, splits, 0, BN};
+    if (info) {
+        *info = LaunchInfo{};
+        info->grid = grid;
+        info->block = kThreads;
+        info->splits = sk.splits;
+        info->tile_n = BN;
+        info->cluster = CL;
+    }
     return TRB_OK;
+}
+
+// How many clusters of `cl` CTAs of one-CTA-per-SM kernels the device runs at
+// once (GPC boundaries: 74 / 33 / 15 clusters of 2 / 4 / 8 on a 148-SM B200).
+// Queried once per device and size with a representative cluster kernel.
+template <typename Kernel>
+static int cluster_capacity(Kernel kernel, size_t smem, int dev, int cl) {
+    static int cache[64][9] = {};
+    const int slot = cl == 2 ? 2 : cl == 4 ? 4 : 8;
+    if (dev >= 0 && dev < 64 && cache[dev][slot] > 0) return cache[dev][slot];
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(cl * 32));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    if (dev >= 0 && dev < 64 && n > 0) cache[dev][slot] = n;
+    return n;
 }
 
 // Split count for the swapped kernel: minimise waves x k-blocks per unit
@@ -1237,51 +1522,128 @@ static int choose_swap_splits(long tiles, int num_kb, int sms) {
     return best;
 }
 
-template <int DT, bool KB, int BS>
+template <int DT, bool KB, int BS, int KD, int CL>
 static int launch_swap(const void* a, const void* b, int m, int n, int k, void* c, float out_scale, int splits,
                        int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
     using Tr = Traits<DT>;
-    using Cfg = SwapCfg<BS>;
+    using Cfg = SwapCfg<BS, KD, CL>;
     constexpr int es = Tr::kEsize;
     CUtensorMap tmW, tmS;
     int rc = KB ? encode_2d(&tmW, b, es, (uint64_t)k, (uint64_t)n, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B)
-                : encode_2d(&tmW, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
+                : encode_2d(&tmW, b, es, (uint64_t)n, (uint64_t)k, 128 / es, KD * kBKBytes / es,
+                            Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
     rc = encode_2d(&tmS, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, BS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != TRB_OK) return rc;
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {
-        TRB_CUDA(cudaFuncSetAttribute(gemm_swap_kernel<DT, KB, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        TRB_CUDA(cudaFuncSetAttribute(gemm_swap_kernel<DT, KB, BS, KD, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)Cfg::kSmem));
         attr_set[dev] = true;
     }
     const long tiles = (n + kBM - 1) / kBM;
     const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
-    if (splits <= 0) splits = choose_swap_splits(tiles, num_kb, sms);
-    splits = std::max(1, std::min(splits, num_kb));
-    const int kbps = (num_kb + splits - 1) / splits;
-    splits = (num_kb + kbps - 1) / kbps;
-    // No K rotation: the A box is only BS x 128 bytes, and CTAs that walk K in
+    // No K rotation: the S box is only BS x 128 bytes, and CTAs that walk K in
     // step read whole rows of B together (measured 29.1 vs 30.7 us at
     // M = 16, N = K = 8192 bf16 with per-tile rotation).
-    SplitK sk{splits, kbps, nullptr, nullptr, 0};
-    if (splits > 1) {
-        rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * BS * sizeof(float), (size_t)tiles, &sk);
-        if (rc != TRB_OK) return rc;
+    SplitK sk{1, num_kb, nullptr, nullptr, 0};
+    int grid;
+    if constexpr (CL > 1) {
+        sk.splits = CL;
+        sk.kb_per_split = (num_kb + CL - 1) / CL;  // the caller checked that every split owns >= 1 k-block
+        grid = (int)(tiles * CL);
+    } else {
+        if (splits <= 0) splits = choose_swap_splits(tiles, num_kb, sms);
+        splits = std::max(1, std::min(splits, num_kb));
+        const int kbps = (num_kb + splits - 1) / splits;
+        splits = (num_kb + kbps - 1) / kbps;
+        sk.splits = splits;
+        sk.kb_per_split = kbps;
+        if (splits > 1) {
+            rc = ensure_workspace(dev, (size_t)tiles * splits * kBM * BS * sizeof(float), (size_t)tiles, &sk);
+            if (rc != TRB_OK) return rc;
+        }
+        grid = (int)std::max<long>(1, std::min<long>(tiles * splits, sms));
     }
-    const long units = tiles * splits;
-    const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
-    gemm_swap_kernel<DT, KB, BS><<<grid, kThreads, Cfg::kSmem, stream>>>(tmW, tmS, c, m, n, k, out_scale, sk);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    int nattr = 0;
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+    if (CL > 1) {
+        attr[nattr].id = cudaLaunchAttributeClusterDimension;
+        attr[nattr].val.clusterDim.x = CL;
+        attr[nattr].val.clusterDim.y = 1;
+        attr[nattr].val.clusterDim.z = 1;
+        ++nattr;
+    }
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = nattr;
+    TRB_CUDA(cudaLaunchKernelEx(&cfg, gemm_swap_kernel<DT, KB, BS, KD, CL>, tmW, tmS, c, m, n, k, out_scale, sk));
     TRB_CUDA(cudaGetLastError());
     if (info) {
         *info = LaunchInfo{};
         info->grid = grid;
         info->block = kThreads;
-        info->splits = splits;
+        info->splits = sk.splits;
         info->tile_n = BS;
         info->swap = 1;
+        info->cluster = CL;
     }
     return TRB_OK;
+}
+
+// Cluster split count for the swapped kernel: the largest of 8, 4, 2 whose
+// tiles x splits CTAs fit on the SMs at once with >= 4 k-blocks per split
+// (every split non-empty); 1 when the panels alone fill most SMs or no count fits.
+template <typename Capacity>
+static int choose_swap_cluster(long tiles, int num_kb, int sms, Capacity capacity) {
+    if (tiles * 2 > sms) return 1;
+    for (int cl : {8, 4, 2}) {
+        const int kbps = (num_kb + cl - 1) / cl;
+        if (tiles * cl <= sms && num_kb >= 4 * cl && (long)(cl - 1) * kbps < num_kb && tiles <= capacity(cl)) return cl;
+    }
+    return 1;
+}
+
+// K-blocks per stage: 2 (MN-major W boxes 2 k-blocks tall measured 4-7% faster
+// than 1; 4 gave no further gain).  cluster: < 0 automatic, 0 = global
+// workspace split-K (`splits`), 2 / 4 / 8 = cluster split-K of that size.
+template <int DT, bool KB, int BS>
+static int launch_swap_kd(int cluster, const void* a, const void* b, int m, int n, int k, void* c, float out_scale,
+                          int splits, int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
+    constexpr int kKD = 2;
+    constexpr int es = Traits<DT>::kEsize;
+    const long tiles = (n + kBM - 1) / kBM;
+    const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
+    int cl = cluster;
+    if (cl < 0) {
+        auto capacity = [dev](int c) {
+            return c == 2   ? cluster_capacity(gemm_swap_kernel<DT, KB, BS, kKD, 2>, SwapCfg<BS, kKD, 2>::kSmem, dev, 2)
+                   : c == 4 ? cluster_capacity(gemm_swap_kernel<DT, KB, BS, kKD, 4>, SwapCfg<BS, kKD, 4>::kSmem, dev, 4)
+                            : cluster_capacity(gemm_swap_kernel<DT, KB, BS, kKD, 8>, SwapCfg<BS, kKD, 8>::kSmem, dev, 8);
+        };
+        cl = splits > 0 ? 1 : choose_swap_cluster(tiles, num_kb, sms, capacity);
+    }
+    if (cl > 1) {
+        const int kbps = (num_kb + cl - 1) / cl;
+        if ((cl != 2 && cl != 4 && cl != 8) || (long)(cl - 1) * kbps >= num_kb) {
+            set_error("trb_gemm_launch: cluster split-K of %d needs every split to own a k-block (%d k-blocks)", cl,
+                      num_kb);
+            return TRB_ERR_ARGS;
+        }
+    }
+    switch (cl) {
+        case 2: return launch_swap<DT, KB, BS, kKD, 2>(a, b, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+        case 4: return launch_swap<DT, KB, BS, kKD, 4>(a, b, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+        case 8: return launch_swap<DT, KB, BS, kKD, 8>(a, b, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+        default: return launch_swap<DT, KB, BS, kKD, 1>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+    }
 }
 
 template <int DT, bool KB>
@@ -1298,9 +1660,11 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
             set_error("trb_gemm_launch: the swapped-operand kernel takes m <= 64 (got %d)", m);
             return TRB_ERR_ARGS;
         }
-        if (m <= 16) return launch_swap<DT, KB, 16>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
-        if (m <= 32) return launch_swap<DT, KB, 32>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
-        return launch_swap<DT, KB, 64>(a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        // splits < 0: cluster split-K of -splits CTAs; > 0: workspace split-K; 0: automatic.
+        const int cluster = splits < 0 ? -splits : (splits > 0 ? 0 : -1);
+        if (m <= 16) return launch_swap_kd<DT, KB, 16>(cluster, a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        if (m <= 32) return launch_swap_kd<DT, KB, 32>(cluster, a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        return launch_swap_kd<DT, KB, 64>(cluster, a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
     }
     // Automatic choice, from sustained clock-normalised measurements on B200
     // (8192^3, TFLOP/s per SM-GHz): the CTA pair (bf16 96%, e4m3 90% of the
@@ -1318,7 +1682,43 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         }
         tile_n_single = tile_n_opt;
     }
-    const bool pair = (cta_pair > 0 || (cta_pair < 0 && tile_n_opt == 0 && tile_n_single == 256)) && sms >= 2;
+    // Cluster split-K of the single-CTA kernel with 256-wide tiles: forced by
+    // splits < 0, automatic when the tiles would leave more than half of the
+    // SMs idle (e.g. M <= 128, N = 8192: 32 tiles x 4 splits) -- each CTA then
+    // streams a quarter of A's K range instead of all of A.
+    const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
+    int cluster = 1;
+    if (splits < 0) {
+        cluster = -splits;
+        const int kbps = (num_kb + cluster - 1) / cluster;
+        if ((cluster != 2 && cluster != 4 && cluster != 8) || cta_pair > 0 || (tile_n_opt > 0 && tile_n_opt != 256) ||
+            (long)(cluster - 1) * kbps >= num_kb) {
+            set_error("trb_gemm_launch: cluster split-K takes 2, 4 or 8 splits of 256-wide single-CTA tiles, each "
+                      "split owning a k-block (splits %d, %d k-blocks)", splits, num_kb);
+            return TRB_ERR_ARGS;
+        }
+        tile_n_single = 256;
+    } else if (splits == 0 && cta_pair < 0 && tile_n_opt == 0) {
+        const long tiles256 = (long)((m + kBM - 1) / kBM) * ((n + 255) / 256);
+        if (tiles256 * 2 <= sms) {
+            auto capacity = [dev](int c) {
+                return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfg<256>::kSmem, dev, 2)
+                       : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfg<256>::kSmem, dev, 4)
+                                : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfg<256>::kSmem, dev, 8);
+            };
+            for (int cl : {8, 4, 2}) {
+                const int kbps = (num_kb + cl - 1) / cl;
+                if (tiles256 * cl <= sms && num_kb >= 4 * cl && (long)(cl - 1) * kbps < num_kb &&
+                    tiles256 <= capacity(cl)) {
+                    cluster = cl;
+                    tile_n_single = 256;
+                    break;
+                }
+            }
+        }
+    }
+    const bool pair =
+        cluster == 1 && (cta_pair > 0 || (cta_pair < 0 && tile_n_opt == 0 && tile_n_single == 256)) && sms >= 2;
     const int tile_n = pair ? kPairN : tile_n_single;
 
     CUtensorMap tmA, tmB;
@@ -1330,6 +1730,9 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     else
         rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
+    if (cluster == 2) return launch_single<DT, KB, 256, 2>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+    if (cluster == 4) return launch_single<DT, KB, 256, 4>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+    if (cluster == 8) return launch_single<DT, KB, 256, 8>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
     if (!pair) {
         if (tile_n == 64) {
             if constexpr (KB || es >= 2)
@@ -1347,7 +1750,6 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     }
     const int workers = sms / 2;
     const long tiles = (long)((m + kPairM - 1) / kPairM) * ((n + kPairN - 1) / kPairN);
-    const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
     if (splits <= 0) splits = choose_splits(tiles, num_kb, workers);
     splits = std::max(1, std::min(splits, num_kb));
     const int kbps = (num_kb + splits - 1) / splits;
@@ -1359,8 +1761,10 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     }
     const long units = tiles * splits;
     const int grid_workers = (int)std::max<long>(1, std::min<long>(units, workers));
-    gemm_tcgen05_pair_kernel<DT, KB><<<grid_workers * 2, kThreads, kPairSmemBytes, stream>>>(tmA, tmB, c, m, n, k,
-                                                                                          out_scale, sk);
+    // The pair kernel's cluster shape (2 CTAs) is compiled in (__cluster_dims__).
+    rc = launch_ex(gemm_tcgen05_pair_kernel<DT, KB>, grid_workers * 2, kPairSmemBytes, 1, stream, tmA, tmB, c, m, n, k,
+                   out_scale, sk);
+    if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaGetLastError());
     if (info) *info = {grid_workers * 2, kThreads, splits, 1, kPairN};
     return TRB_OK;
@@ -1473,8 +1877,8 @@ int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c
         set_error("trb_gemm_launch: A, B and C must be 16-byte aligned");
         return TRB_ERR_ALIGN;
     }
-    if (splits < 0) {
-        set_error("trb_gemm_launch: splits must be >= 0");
+    if (splits < 0 && splits != -2 && splits != -4 && splits != -8) {
+        set_error("trb_gemm_launch: splits must be >= 0, or -2 / -4 / -8 for cluster split-K (got %d)", splits);
         return TRB_ERR_ARGS;
     }
     if (dtype == TRB_FLOAT32) return launch_fp32x3(m, n, k, a, b, c, splits, cta_pair, tile_n, b_kmajor, stream, info);

@@ -50,12 +50,15 @@ struct LaunchInfo {
     int fp32x3 = 0;   // float32 computed as three tf32 products
     int fp64 = 0;     // float64 CUDA-core kernel
     int swap = 0;     // swapped-operand skinny kernel (C^T = B^T A^T); tile_n = its MMA N
+    int cluster = 1;  // > 1: K splits reduced inside a thread-block cluster of that size
 };
 // splits: 0 = automatic (split-K only for problems that leave SMs idle), >= 1 forced.
 // cta_pair: < 0 automatic (pair, or narrow single-CTA tiles when skinny), 0 single-CTA, > 0 CTA pair.
 // b_kmajor: B is stored N x K (K-major) instead of the row-major K x N matrix.
 // tile_n: 0 automatic; 64 / 128 / 256 force the single-CTA kernel at that tile
-// width; < 0 forces the swapped-operand kernel (m <= 64).
+// width; < 0 forces the swapped-operand kernel (m <= 64): -1 with the
+// workspace split-K of `splits` (0 = automatic), -2 / -4 / -8 with cluster
+// split-K of that size.
 int launch(int dtype, int m, int n, int k, const void* a, const void* b, void* c, float scale_a, float scale_b,
            int splits, int cta_pair, int b_kmajor, cudaStream_t stream, LaunchInfo* info, int tile_n = 0);
 int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsigned int* absmax_scratch,
@@ -278,6 +281,31 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
         if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
     }
 }
+// Programmatic dependent launch.  wait: block until the grids this one
+// depends on have completed and their memory is visible (a no-op without a
+// programmatic dependency).  launch_dependents: allow the next grid in the
+// stream to be scheduled (its own wait still orders its memory accesses).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// 16-byte store into another CTA's shared memory (address from mapa_shared).
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+// Asynchronous 16-byte store into another CTA's shared memory; its bytes
+// complete on `cluster_bar`, an mbarrier in the same destination CTA.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint4 v, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     cluster_addr),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(cluster_bar)
+                 : "memory");
+}
+
 // The pair's even CTA (rank 0) owns the barriers that both CTAs' TMA loads
 // complete on; clearing bit 24 of a shared::cluster address selects it.
 constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;

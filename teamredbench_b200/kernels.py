@@ -74,9 +74,11 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     tf32 products, float64 on the CUDA cores).  Output dtypes: bf16 for bf16 /
     e4m3 inputs, f16 for f16, f32 for tf32 and float32, f64 for float64, int32
     for int8.
-    splits: 0 = automatic split-K, >= 1 forces that many K splits.
+    splits: 0 = automatic split-K, >= 1 forces that many K splits reduced
+    through a global workspace, -2 / -4 / -8 that many splits reduced inside a
+    thread-block cluster (distributed shared memory).
     cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel.
-    tile_n: 0 automatic, 64/128/256 single-CTA tile width, < 0 the
+    tile_n: 0 automatic, 64/128/256 single-CTA tile width, -1 the
     swapped-operand skinny kernel (C^T = B^T A^T, m <= 64; automatic for
     m <= 64)."""
     _require_cuda_contiguous(a, b, out)

@@ -145,13 +145,13 @@ def test_pair_and_single_agree_bitwise_for_int8():
 
 
 def test_split_k_run_entry_reports_splits():
-    res = _native.gemm_run("bfloat16", 16, 1024, 8192, 1, 3)  # 8 swapped panels: K is split 16 ways
-    assert res.split_k == 16 and res.device_error == 0
-    assert res.implementation.decode() == "tcgen05_swap_128x16_splitk"
-    res = _native.gemm_run("bfloat16", 16, 8192, 8192, 1, 3)  # 64 panels x 2 splits
-    assert res.split_k == 2 and res.implementation.decode() == "tcgen05_swap_128x16_splitk"
-    res = _native.gemm_run("bfloat16", 128, 8192, 8192, 1, 3)  # 128 narrow tiles: no split needed
-    assert res.split_k == 1 and res.implementation.decode() == "tcgen05_1cta_128x64"
+    res = _native.gemm_run("bfloat16", 16, 1024, 8192, 1, 3)  # 8 swapped panels x clusters of 8 K splits
+    assert res.split_k == 8 and res.device_error == 0
+    assert res.implementation.decode() == "tcgen05_swap_128x16_cluster8"
+    res = _native.gemm_run("bfloat16", 16, 8192, 8192, 1, 3)  # 64 panels x clusters of 2
+    assert res.split_k == 2 and res.implementation.decode() == "tcgen05_swap_128x16_cluster2"
+    res = _native.gemm_run("bfloat16", 128, 8192, 8192, 1, 3)  # 32 tiles x clusters of 4 K splits
+    assert res.split_k == 4 and res.implementation.decode() == "tcgen05_1cta_128x256_cluster4"
     res = _native.gemm_run("bfloat16", 4096, 4096, 4096, 1, 3)
     assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x256"
     res = _native.gemm_run("float8_e4m3fn", 4096, 4096, 4096, 1, 3)
@@ -371,3 +371,67 @@ def test_swap_kernel_is_automatic_for_m_le_64_and_validates_options():
     assert res.implementation.decode().startswith("tcgen05_swap_128x64") and res.device_error == 0
     res = _native.gemm_run("float32", 32, 4096, 4096, 1, 2)
     assert res.implementation.decode().startswith("fp32x3_tcgen05_swap_128x32") and res.device_error == 0
+
+
+@pytest.mark.parametrize("name", DTYPES)
+@pytest.mark.parametrize("shape", [(16, 8192, 8192), (32, 1024, 4096), (64, 2048, 2048), (5, 256, 1024),
+                                   (48, 528, 3072)])
+@pytest.mark.parametrize("cluster", [2, 4, 8])
+@pytest.mark.parametrize("b_transposed", [False, True])
+def test_swap_cluster_split_k(name, shape, cluster, b_transposed):
+    """Cluster split-K (partials reduced through distributed shared memory)
+    against the oracle, and bit-identical to the workspace split-K with the
+    same split count (same K partition, same summation order)."""
+    m, n, k = shape
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=m + 2 * n + k)
+    bb = b.t().contiguous() if b_transposed else b
+    c_cl = torch.empty((m, n), device="cuda", dtype=torch_dtype(GEMM_OUT[name]))
+    c_ws = torch.empty_like(c_cl)
+    num_kb = -(-k * b.element_size() // 128)
+    kbps = -(-num_kb // cluster)
+    if (cluster - 1) * kbps >= num_kb:
+        with pytest.raises(_native.NativeError):
+            gemm(a, bb, c_cl, dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, tile_n=-1, splits=-cluster)
+        return
+    gemm(a, bb, c_cl, dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, tile_n=-1, splits=-cluster)
+    gemm(a, bb, c_ws, dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, tile_n=-1, splits=cluster)
+    torch.cuda.synchronize()
+    assert torch.equal(c_cl, c_ws)
+    _check(name, a, b, c_cl, sa, sb, np.arange(m), tol=gemm_tolerance(name, k))  # splitting only shortens the chains
+
+
+@pytest.mark.parametrize("name", DTYPES)
+@pytest.mark.parametrize("shape", [(128, 8192, 8192), (100, 2048, 4096), (65, 528, 3072), (256, 1024, 2048),
+                                   (129, 272, 1024)])
+@pytest.mark.parametrize("cluster", [2, 4, 8])
+@pytest.mark.parametrize("b_transposed", [False, True])
+def test_tile_kernel_cluster_split_k(name, shape, cluster, b_transposed):
+    """Cluster split-K of the 128 x 256 single-CTA kernel (column blocks of
+    the tile reduced through distributed shared memory) vs the oracle, and
+    bit-identical to the workspace split-K with the same split count."""
+    m, n, k = shape
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=m + 3 * n + k)
+    bb = b.t().contiguous() if b_transposed else b
+    c_cl = torch.empty((m, n), device="cuda", dtype=torch_dtype(GEMM_OUT[name]))
+    c_ws = torch.empty_like(c_cl)
+    num_kb = -(-k * b.element_size() // 128)
+    kbps = -(-num_kb // cluster)
+    kw = dict(dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, cta_pair=0, tile_n=256)
+    if (cluster - 1) * kbps >= num_kb:
+        with pytest.raises(_native.NativeError):
+            gemm(a, bb, c_cl, splits=-cluster, **kw)
+        return
+    gemm(a, bb, c_cl, splits=-cluster, **kw)
+    gemm(a, bb, c_ws, splits=cluster, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(c_cl, c_ws)
+    rows = np.arange(m) if m <= 256 else np.sort(np.random.default_rng(0).choice(m, 128, replace=False))
+    _check(name, a, b, c_cl, sa, sb, rows, tol=gemm_tolerance(name, k))  # splitting only shortens the chains
+
+
+def test_cluster_split_k_option_errors():
+    a, b, _, _ = gemm_operands("bfloat16", 128, 512, 256, seed=1)  # 4 k-blocks
+    c = torch.empty((128, 512), device="cuda", dtype=torch.bfloat16)
+    for kw in ({"splits": -3}, {"splits": -8}, {"splits": -2, "cta_pair": 1}, {"splits": -2, "tile_n": 128}):
+        with pytest.raises(_native.NativeError):
+            gemm(a, b, c, **kw)
