@@ -289,7 +289,8 @@ def run_b200(args) -> None:
 
 
 def secondary_measurements(torch, dev, stream, peaks) -> dict:
-    """bf16 triad, fp32 copy/scale and the 8192^3 bf16 / fp8 GEMMs (config[1], [3])."""
+    """bf16 triad, fp32 copy/scale, the 8192^3 bf16 / fp8 GEMMs, the skinny bf16
+    GEMMs and float32 / float64 8192^3 (configs[1]-[3])."""
     from teamredbench_b200 import _native
     from teamredbench_b200.kernels import gemm, stream_op
 
@@ -342,6 +343,50 @@ def secondary_measurements(torch, dev, stream, peaks) -> dict:
         out[f"gemm_{name}_8192_mfu_pct_nominal"] = round(100 * tflops / nominal[name], 2)
         if name == "bfloat16":
             out["gemm_bfloat16_8192_frac_of_measured_cublas_burst"] = round(tflops / peaks["bf16_tflops"], 4)
+        del a, b, c
+        torch.cuda.empty_cache()
+    # Skinny shapes (configs[3]: M = 16 / 128, N = K = 8192, bf16): HBM-bound, so
+    # report the byte rate against the measured copy peak.  20 launches replayed
+    # from a CUDA graph (the Python wrapper's host cost would otherwise show).
+    def graph_timed(fn, reps=20, iters=5):
+        fn()
+        torch.cuda.synchronize(dev)
+        cap = torch.cuda.Stream(dev)
+        with torch.cuda.stream(cap):
+            fn()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=cap):
+                for _ in range(reps):
+                    fn()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        e.record(stream)
+        torch.cuda.synchronize(dev)
+        del graph
+        return s.elapsed_time(e) / 1e3 / (reps * iters)
+
+    for m in (16, 128):
+        a = (torch.randn(m, k, generator=g, device=dev) / k ** 0.5).to(torch.bfloat16)
+        b = (torch.randn(k, n, generator=g, device=dev) / k ** 0.5).to(torch.bfloat16)
+        c = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+        t = graph_timed(lambda: gemm(a, b, c))
+        moved = (m * k + k * n + m * n) * 2
+        out[f"gemm_bfloat16_skinny_m{m}_us"] = round(t * 1e6, 2)
+        out[f"gemm_bfloat16_skinny_m{m}_frac_of_measured_hbm"] = round(moved / t / 1e9 / peaks["hbm_gbs"], 4)
+        del a, b, c
+    # float32 (three tf32 products) and float64 (CUDA cores) at 8192^3 -- the
+    # reference's high-precision native path.
+    for name, torch_dt in (("float32", torch.float32), ("float64", torch.float64)):
+        a = torch.randn(8192, 8192, generator=g, device=dev, dtype=torch_dt) / 8192 ** 0.5
+        b = torch.randn(8192, 8192, generator=g, device=dev, dtype=torch_dt) / 8192 ** 0.5
+        c = torch.empty_like(a)
+        t = timed(lambda: gemm(a, b, c), iters=5 if name == "float64" else 10, warm=2)
+        out[f"gemm_{name}_8192_tflops"] = round(2.0 * 8192 ** 3 / t / 1e12, 1)
         del a, b, c
         torch.cuda.empty_cache()
     if _native.device_error(dev.index, clear=True):
