@@ -184,8 +184,8 @@ int trb_gemm_run(const trb_gemm_args* args, trb_result* out);
  * uses the upper 19 bits of each f32 input.  float32 runs on the tf32 tensor
  * cores as three products (x = hi + lo, C = A_lo B_hi + A_hi B_lo + A_hi B_hi;
  * one split pass per operand into a library workspace of 12 (mk + kn) bytes);
- * float64 runs on CUDA cores (no tensor-core kind takes fp64) and needs only
- * 8-byte aligned pointers.  Others require k * elem % 16 == 0,
+ * float64 runs on the DMMA tensor path (mma.sync m8n8k4 f64; no tcgen05 kind
+ * takes fp64) and needs only 8-byte aligned pointers.  Others require k * elem % 16 == 0,
  * n * elem % 16 == 0 and 16-byte aligned pointers (TMA); any m, n, k > 0
  * otherwise.  Replaces
  * the reference's torch.mm(a, b, out=out) (src/teamredbench/benchmarks/mfu.py:

@@ -337,7 +337,7 @@ static size_t gemm_out_size(int dtype) {
 
 static void gemm_impl_name(const gemm::LaunchInfo& info, char* out, size_t size, const char* suffix) {
     if (info.fp64) {
-        snprintf(out, size, "fp64_fma_128x128%s", suffix);
+        snprintf(out, size, "fp64_dmma_128x128%s", suffix);
         return;
     }
     snprintf(out, size, "%stcgen05_%s_%dx%d%s%s", info.fp32x3 ? "fp32x3_" : "",

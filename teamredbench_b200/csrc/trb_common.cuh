@@ -48,7 +48,7 @@ namespace gemm {
 struct LaunchInfo {
     int grid = 0, block = 0, splits = 1, pair = 0, tile_n = 256;
     int fp32x3 = 0;   // float32 computed as three tf32 products
-    int fp64 = 0;     // float64 CUDA-core kernel
+    int fp64 = 0;     // float64 DMMA kernel
     int swap = 0;     // swapped-operand skinny kernel (C^T = B^T A^T); tile_n = its MMA N
     int cluster = 1;  // > 1: K splits reduced inside a thread-block cluster of that size
 };
@@ -67,7 +67,7 @@ int read_error(bool clear);
 }  // namespace gemm
 
 namespace dgemm {
-// float64 C = A * B on CUDA cores (no tcgen05 kind takes fp64); any m, n, k.
+// float64 C = A * B on the DMMA tensor path (no tcgen05 kind takes fp64); any m, n, k.
 int launch(int m, int n, int k, const void* a, const void* b, void* c, int b_kmajor, cudaStream_t stream,
            gemm::LaunchInfo* info);
 }  // namespace dgemm

@@ -71,7 +71,7 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
 
     dtype defaults to the tensors' dtype; pass ``dtype="tfloat32"`` to run
     float32 tensors on the tf32 tensor-core path (float32 itself runs as three
-    tf32 products, float64 on the CUDA cores).  Output dtypes: bf16 for bf16 /
+    tf32 products, float64 on the DMMA tensor path).  Output dtypes: bf16 for bf16 /
     e4m3 inputs, f16 for f16, f32 for tf32 and float32, f64 for float64, int32
     for int8.
     splits: 0 = automatic split-K, >= 1 forces that many K splits reduced
