@@ -1389,13 +1389,66 @@ static int choose_splits(long tiles, int num_kb, int sms) {
     return (int)std::max<long>(1, std::min<long>(s, 16));
 }
 
-// Narrowest single-CTA tile width for skinny problems: one row of 128-row
-// tiles that, at BN = 256, would leave more than half of the SMs idle.  8-bit
-// MN-major B needs BN >= 128 (one 128-byte swizzle row holds 128 elements).
-static int choose_tile_n(int m, int n, int es, bool kb, int sms) {
-    const long tiles256 = (long)((m + kBM - 1) / kBM) * ((n + 255) / 256);
-    if (m > kBM || tiles256 * 2 > sms) return 256;
-    return (es >= 2 || kb) ? 64 : 128;
+
+// Automatic kernel choice for M > 64: the candidate with the highest
+//   (work units / (waves x slots)) x per-tile efficiency,
+// where slots are the SMs (single CTA) or SM pairs (CTA pair).  Per-tile
+// factors, relative to the CTA pair, calibrated on B200 (bf16 and e4m3,
+// 1024^3 ... 16384^3, CUDA-graph timing): 128 x 256 single-CTA tiles 0.89,
+// 128 x 128 0.72, 128 x 64 0.50.  A CTA that owns one tile cannot hide its
+// pipeline fill and epilogue behind a next tile, which costs the pair (heavier
+// setup) its edge on a short K loop: the pair's factor is 0.85 when it runs a
+// single wave with < 40 k-blocks (bf16 2048^3: 128 x 256 tiles 1099 TFLOP/s
+// vs the pair 1031; e4m3 4096^3, four waves: the pair 2721 vs 2499).
+// Cluster split-K (256-wide tiles, x 0.85 for its exchange) is a candidate
+// only when every split keeps >= 16 k-blocks and all clusters are
+// co-resident.  Workspace split-K lost in every measured case; it is used
+// only when no candidate fills a quarter of the slots and K is long
+// (>= 256 k-blocks, e.g. 256 x 256 x 65536), where its fix-up amortises.
+// Picks: 1024^3 -> 128 x 64, 1536^3 -> 128 x 128, 2048^3 -> 128 x 256,
+// >= 2560^3 -> pair, M = 128 x N = K = 8192 -> 128 x 256 with clusters of 4.
+struct KernelChoice {
+    bool pair;
+    int tile_n;
+    int cluster;
+    double score;
+};
+template <typename Capacity>
+static KernelChoice choose_kernel(int m, int n, int num_kb, bool allow_bn64, int sms, Capacity capacity) {
+    auto wave_eff = [](long units, long slots) {
+        if (units <= 0 || slots <= 0) return 0.0;
+        const long waves = (units + slots - 1) / slots;
+        return (double)units / (double)(waves * slots);
+    };
+    const long mb = (m + kBM - 1) / kBM;
+    KernelChoice best{sms >= 2, 256, 1, 0.0};
+    double best_score = -1.0;
+    if (sms >= 2) {
+        const long tiles = (long)((m + kPairM - 1) / kPairM) * ((n + kPairN - 1) / kPairN);
+        const bool one_wave = tiles <= sms / 2;
+        best_score = wave_eff(tiles, sms / 2) * (one_wave && num_kb < 40 ? 0.85 : 1.0);
+    }
+    for (int bn : {256, 128, 64}) {
+        if (bn == 64 && !allow_bn64) continue;
+        const double f = bn == 256 ? 0.89 : bn == 128 ? 0.72 : 0.50;
+        const double score = wave_eff(mb * ((n + bn - 1) / bn), sms) * f;
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best = {false, bn, 1, score};
+        }
+    }
+    const long tiles256 = mb * ((n + 255) / 256);
+    for (int cl : {2, 4, 8}) {
+        const int kbps = (num_kb + cl - 1) / cl;
+        if (kbps < 16 || (long)(cl - 1) * kbps >= num_kb || tiles256 > capacity(cl)) continue;
+        const double score = wave_eff(tiles256 * cl, sms) * 0.89 * 0.85;
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best = {false, 256, cl, score};
+        }
+    }
+    best.score = best_score;
+    return best;
 }
 
 // Launch with programmatic stream serialization (the kernels' griddepcontrol
@@ -1666,11 +1719,9 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         if (m <= 32) return launch_swap_kd<DT, KB, 32>(cluster, a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
         return launch_swap_kd<DT, KB, 64>(cluster, a, b, m, n, k, c, out_scale, splits, dev, sms, stream, info);
     }
-    // Automatic choice, from sustained clock-normalised measurements on B200
-    // (8192^3, TFLOP/s per SM-GHz): the CTA pair (bf16 96%, e4m3 90% of the
-    // per-clock tensor peak, vs 83% / 79% for one CTA), except for skinny
-    // problems, which take narrow single-CTA tiles.
-    int tile_n_single = choose_tile_n(m, n, es, KB, sms);
+    // Forced choices first (tile_n, splits, cta_pair); the automatic choice is
+    // choose_kernel's wave model below.
+    int tile_n_single = 256;
     if (tile_n_opt > 0) {
         if (tile_n_opt != 64 && tile_n_opt != 128 && tile_n_opt != 256) {
             set_error("trb_gemm_launch: tile_n must be 64, 128 or 256 (got %d)", tile_n_opt);
@@ -1682,13 +1733,11 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         }
         tile_n_single = tile_n_opt;
     }
-    // Cluster split-K of the single-CTA kernel with 256-wide tiles: forced by
-    // splits < 0, automatic when the tiles would leave more than half of the
-    // SMs idle (e.g. M <= 128, N = 8192: 32 tiles x 4 splits) -- each CTA then
-    // streams a quarter of A's K range instead of all of A.
     const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
     int cluster = 1;
+    bool pair_auto = false;
     if (splits < 0) {
+        // Cluster split-K of the single-CTA kernel with 256-wide tiles.
         cluster = -splits;
         const int kbps = (num_kb + cluster - 1) / cluster;
         if ((cluster != 2 && cluster != 4 && cluster != 8) || cta_pair > 0 || (tile_n_opt > 0 && tile_n_opt != 256) ||
@@ -1699,26 +1748,20 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         }
         tile_n_single = 256;
     } else if (splits == 0 && cta_pair < 0 && tile_n_opt == 0) {
-        const long tiles256 = (long)((m + kBM - 1) / kBM) * ((n + 255) / 256);
-        if (tiles256 * 2 <= sms) {
-            auto capacity = [dev](int c) {
-                return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfg<256>::kSmem, dev, 2)
-                       : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfg<256>::kSmem, dev, 4)
-                                : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfg<256>::kSmem, dev, 8);
-            };
-            for (int cl : {8, 4, 2}) {
-                const int kbps = (num_kb + cl - 1) / cl;
-                if (tiles256 * cl <= sms && num_kb >= 4 * cl && (long)(cl - 1) * kbps < num_kb &&
-                    tiles256 <= capacity(cl)) {
-                    cluster = cl;
-                    tile_n_single = 256;
-                    break;
-                }
-            }
-        }
+        auto capacity = [dev](int c) {
+            return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfg<256>::kSmem, dev, 2)
+                   : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfg<256>::kSmem, dev, 4)
+                            : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfg<256>::kSmem, dev, 8);
+        };
+        const KernelChoice kc = choose_kernel(m, n, num_kb, KB || es >= 2, sms, capacity);
+        pair_auto = kc.pair;
+        tile_n_single = kc.tile_n;
+        cluster = kc.cluster;
+        if (kc.score >= 0.25 || num_kb < 256) splits = 1;  // else: workspace split-K count chosen below
+    } else if (cta_pair < 0 && tile_n_opt == 0) {
+        pair_auto = true;  // explicit workspace split-K count: the pair, as before
     }
-    const bool pair =
-        cluster == 1 && (cta_pair > 0 || (cta_pair < 0 && tile_n_opt == 0 && tile_n_single == 256)) && sms >= 2;
+    const bool pair = cluster == 1 && (cta_pair > 0 || pair_auto) && sms >= 2;
     const int tile_n = pair ? kPairN : tile_n_single;
 
     CUtensorMap tmA, tmB;

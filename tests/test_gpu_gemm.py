@@ -435,3 +435,21 @@ def test_cluster_split_k_option_errors():
     for kw in ({"splits": -3}, {"splits": -8}, {"splits": -2, "cta_pair": 1}, {"splits": -2, "tile_n": 128}):
         with pytest.raises(_native.NativeError):
             gemm(a, b, c, **kw)
+
+
+@pytest.mark.parametrize("size,impl", [(1024, "tcgen05_1cta_128x64"), (1536, "tcgen05_1cta_128x128"),
+                                       (2048, "tcgen05_1cta_128x256"), (3072, "tcgen05_cta_pair_256x256"),
+                                       (8192, "tcgen05_cta_pair_256x256")])
+def test_automatic_kernel_choice_for_square_sizes(size, impl):
+    """The wave model's picks for the BASELINE square sweep (tiles that fill
+    the SMs in whole waves; the pair once the grid is large and K long)."""
+    res = _native.gemm_run("bfloat16", size, size, size, 0, 1)
+    assert res.implementation.decode() == impl and res.split_k == 1 and res.device_error == 0
+
+
+@pytest.mark.parametrize("shape", [(1024, 1024, 1024), (1536, 1536, 1536), (2048, 2048, 2048)])
+def test_small_square_auto_choice_matches_oracle(shape):
+    m, n, k = shape
+    a, b, _, _ = gemm_operands("bfloat16", m, n, k, seed=k)
+    c = _run("bfloat16", a, b)
+    _check("bfloat16", a, b, c, 1.0, 1.0, np.sort(np.random.default_rng(k).choice(m, 96, replace=False)))
