@@ -49,7 +49,6 @@ constexpr int kBStage = kBN * kBKBytes;  // 32 KiB
 constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kNumAcc * kBN;  // 512
 constexpr int kThreads = 192;
-constexpr int kGroupM = 16;
 constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBStage) + 1024;  // + alignment slack
 
 // Single-CTA tile-width variants: BN = 256 (default), 128 and 64 (skinny
@@ -147,7 +146,8 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
     else mma_i8(d, a, b, idesc, acc);
 }
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb, int& nb) {
+    const int kGroupM = group_m > 0 ? group_m : 16;
     const int group = kGroupM * num_n;
     const int g = tile / group;
     const int first_m = g * kGroupM;
@@ -216,6 +216,7 @@ struct SplitK {
     float* ws;
     unsigned int* counters;
     int rotate_k;  // 1: start each tile's K loop at k-block (tile % nk) and wrap
+    int group_m;   // m-blocks per raster group (consecutive tiles walk down a group's column)
 };
 
 // K order of a unit: with rotate_k, tiles that run at the same time start at
@@ -315,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
                 int mb, nb;
-                tile_coords(unit / sk.splits, num_m, num_n, mb, nb);
+                tile_coords(unit / sk.splits, num_m, num_n, sk.group_m, mb, nb);
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
                 const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
                 const int rot = k_rotation(sk, unit / sk.splits, nk);
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++t_local) {
             const int tile = unit / sk.splits;
             int mb, nb;
-            tile_coords(tile, num_m, num_n, mb, nb);
+            tile_coords(tile, num_m, num_n, sk.group_m, mb, nb);
             const int acc = t_local & 1;
             const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
             bool ok = mbar_wait(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
@@ -564,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (epi && ok) {
             int mb, nb;
-            tile_coords((int)blockIdx.x / CL, num_m, num_n, mb, nb);
+            tile_coords((int)blockIdx.x / CL, num_m, num_n, sk.group_m, mb, nb);
             const int grow = mb * kBM + row_in_tile;
             const float4* recv = reinterpret_cast<const float4*>(smem_raw + (sRecv - smem_u32(smem_raw)));
             if (grow < M) {
@@ -1103,7 +1104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int unit = pair; ok && unit < num_units; unit += num_pairs) {
                 int mb, nb;
-                tile_coords(unit / sk.splits, num_m, num_n, mb, nb);
+                tile_coords(unit / sk.splits, num_m, num_n, sk.group_m, mb, nb);
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
                 const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
                 for (int kb = kb0; kb < kb1; ++kb) {
@@ -1199,7 +1200,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int unit = pair; unit < num_units; unit += num_pairs, ++t_local) {
             const int tile = unit / sk.splits;
             int mb, nb;
-            tile_coords(tile, num_m, num_n, mb, nb);
+            tile_coords(tile, num_m, num_n, sk.group_m, mb, nb);
             const int acc = t_local & 1;
             const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
             bool ok = mbar_wait_cluster(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
@@ -1451,6 +1452,18 @@ static KernelChoice choose_kernel(int m, int n, int num_kb, bool allow_bn64, int
     return best;
 }
 
+// Raster group: consecutive tiles walk down `group` m-blocks of one column
+// of tiles, so the group's A rows and one B column panel are what the
+// running tiles share in L2.  8 m-blocks measured best on B200 for the CTA
+// pair at 8192^3 and 16384^3 (bf16 1520 / 1514 TFLOP/s vs 1482 / 1465 with 16,
+// 1487 / 1419 with 4); the group's A rows are further kept under ~80 MB of
+// the 126 MB L2 for very long K.
+static int raster_group(int rows_per_block, int k, int es) {
+    const double a_bytes = (double)rows_per_block * k * es;
+    const int g = (int)(80.0e6 / a_bytes);
+    return std::max(2, std::min(8, g));
+}
+
 // Launch with programmatic stream serialization (the kernels' griddepcontrol
 // waits order their global accesses after the previous grid) and, for
 // cluster split-K, the cluster shape.
@@ -1492,7 +1505,7 @@ static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, 
     }
     const long tiles = (long)((m + kBM - 1) / kBM) * ((n + BN - 1) / BN);
     const int num_kb = (int)(((long)k * Tr::kEsize + kBKBytes - 1) / kBKBytes);
-    SplitK sk{1, num_kb, nullptr, nullptr, m <= kBM ? 1 : 0};
+    SplitK sk{1, num_kb, nullptr, nullptr, m <= kBM ? 1 : 0, raster_group(kBM, k, Tr::kEsize)};
     int grid;
     if constexpr (CL > 1) {
         sk.splits = CL;
@@ -1797,7 +1810,7 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     splits = std::max(1, std::min(splits, num_kb));
     const int kbps = (num_kb + splits - 1) / splits;
     splits = (num_kb + kbps - 1) / kbps;
-    SplitK sk{splits, kbps, nullptr, nullptr, 0};
+    SplitK sk{splits, kbps, nullptr, nullptr, 0, raster_group(kPairM, k, es)};
     if (splits > 1) {
         rc = ensure_workspace(dev, (size_t)tiles * splits * 2 * kBM * kPairN * sizeof(float), (size_t)tiles * 2, &sk);
         if (rc != TRB_OK) return rc;
