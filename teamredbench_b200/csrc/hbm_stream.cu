@@ -174,8 +174,15 @@ struct OpTriadF16 {
 };
 
 // ------------------------------------------------------------------ VEC path
-constexpr int kVecThreads = 512;
-constexpr int kVecUnroll = 4;
+// 1024 threads per CTA, two CTAs per SM (64 warps; <= 32 registers per thread,
+// hence the launch bound).  Vectors per array per thread: 2 for triad (two
+// input streams), 4 for copy / scale (one input stream, so the same bytes in
+// flight per SM).  Measured on B200 for the fp32 triad against 512 x 4,
+// 256/512 x 8, 1024 x 4/8, 768 x 4 and 256-bit (v8) loads: 7117 GB/s vs
+// 7049 for 512 x 4 and <= 7080 for the others.
+constexpr int kVecThreads = 1024;
+template <class Op>
+constexpr int vec_unroll() { return Op::kAux ? 2 : 4; }
 
 // Elements [tail_begin, n) that do not fill a 16-byte vector, done by the last CTA.
 template <class Op, class T>
@@ -186,7 +193,7 @@ __device__ __forceinline__ void tail_elems(T* dst, const T* src, const T* aux, u
 }
 
 template <class Op, class T, int U>
-__global__ void __launch_bounds__(kVecThreads) hbm_vec_kernel(T* __restrict__ dst, const T* __restrict__ src,
+__global__ void __launch_bounds__(kVecThreads, 2048 / kVecThreads) hbm_vec_kernel(T* __restrict__ dst, const T* __restrict__ src,
                                                               const T* __restrict__ aux, uint64_t n, Op op) {
     constexpr uint64_t kPerVec = 16 / sizeof(T);
     const uint64_t nvec = n / kPerVec;
@@ -396,6 +403,7 @@ static int launch_op(int variant, T* dst, const T* src, const T* aux, uint64_t n
     // B200 than any persistent grid-stride size (copy 6.92, triad 7.00 TB/s vs
     // <= 6.70 TB/s at 64 CTAs/SM).  blocks_per_sm > 0 caps the grid at
     // sms * blocks_per_sm (grid-stride), the reference's --blocks-per-cu knob.
+    constexpr int kVecUnroll = vec_unroll<Op>();
     const uint64_t tiles = (n * sizeof(T) / 16 + (uint64_t)kVecThreads * kVecUnroll - 1) /
                            ((uint64_t)kVecThreads * kVecUnroll);
     const uint64_t cap = blocks_per_sm > 0 ? (uint64_t)sms * blocks_per_sm : tiles;
