@@ -150,8 +150,8 @@ def test_split_k_run_entry_reports_splits():
     assert res.implementation.decode() == "tcgen05_swap_128x16_cluster8"
     res = _native.gemm_run("bfloat16", 16, 8192, 8192, 1, 3)  # 64 panels x clusters of 2
     assert res.split_k == 2 and res.implementation.decode() == "tcgen05_swap_128x16_cluster2"
-    res = _native.gemm_run("bfloat16", 128, 8192, 8192, 1, 3)  # 32 tiles x clusters of 4 K splits
-    assert res.split_k == 4 and res.implementation.decode() == "tcgen05_1cta_128x256_cluster4"
+    res = _native.gemm_run("bfloat16", 128, 8192, 8192, 1, 3)  # 64 tiles x clusters of 2 K splits
+    assert res.split_k == 2 and res.implementation.decode() == "tcgen05_1cta_128x128_cluster2"
     res = _native.gemm_run("bfloat16", 4096, 4096, 4096, 1, 3)
     assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x256"
     res = _native.gemm_run("float8_e4m3fn", 4096, 4096, 4096, 1, 3)
@@ -405,10 +405,12 @@ def test_swap_cluster_split_k(name, shape, cluster, b_transposed):
                                    (129, 272, 1024)])
 @pytest.mark.parametrize("cluster", [2, 4, 8])
 @pytest.mark.parametrize("b_transposed", [False, True])
-def test_tile_kernel_cluster_split_k(name, shape, cluster, b_transposed):
-    """Cluster split-K of the 128 x 256 single-CTA kernel (column blocks of
-    the tile reduced through distributed shared memory) vs the oracle, and
-    bit-identical to the workspace split-K with the same split count."""
+@pytest.mark.parametrize("tile_n", [256, 128])
+def test_tile_kernel_cluster_split_k(name, shape, cluster, b_transposed, tile_n):
+    """Cluster split-K of the 128 x 256 / 128 x 128 single-CTA kernel (column
+    blocks of the tile reduced through distributed shared memory) vs the
+    oracle, and bit-identical to the workspace split-K with the same split
+    count."""
     m, n, k = shape
     a, b, sa, sb = gemm_operands(name, m, n, k, seed=m + 3 * n + k)
     bb = b.t().contiguous() if b_transposed else b
@@ -416,8 +418,8 @@ def test_tile_kernel_cluster_split_k(name, shape, cluster, b_transposed):
     c_ws = torch.empty_like(c_cl)
     num_kb = -(-k * b.element_size() // 128)
     kbps = -(-num_kb // cluster)
-    kw = dict(dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, cta_pair=0, tile_n=256)
-    if (cluster - 1) * kbps >= num_kb:
+    kw = dict(dtype=name, scale_a=sa, scale_b=sb, b_transposed=b_transposed, cta_pair=0, tile_n=tile_n)
+    if (cluster - 1) * kbps >= num_kb or (tile_n // cluster) % 32:
         with pytest.raises(_native.NativeError):
             gemm(a, bb, c_cl, splits=-cluster, **kw)
         return
@@ -432,7 +434,8 @@ def test_tile_kernel_cluster_split_k(name, shape, cluster, b_transposed):
 def test_cluster_split_k_option_errors():
     a, b, _, _ = gemm_operands("bfloat16", 128, 512, 256, seed=1)  # 4 k-blocks
     c = torch.empty((128, 512), device="cuda", dtype=torch.bfloat16)
-    for kw in ({"splits": -3}, {"splits": -8}, {"splits": -2, "cta_pair": 1}, {"splits": -2, "tile_n": 128}):
+    for kw in ({"splits": -3}, {"splits": -8}, {"splits": -2, "cta_pair": 1}, {"splits": -2, "tile_n": 64},
+               {"splits": -8, "tile_n": 128}):
         with pytest.raises(_native.NativeError):
             gemm(a, b, c, **kw)
 
