@@ -25,6 +25,10 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
+# The contract is one JSON line on stdout; NCCL's own log lines (its version
+# banner when NCCL_DEBUG is set in the environment) go to stderr instead.
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
