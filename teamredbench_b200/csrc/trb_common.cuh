@@ -290,13 +290,6 @@ __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// 16-byte store into another CTA's shared memory (address from mapa_shared).
-__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
-    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x), "r"(v.y), "r"(v.z),
-                 "r"(v.w)
-                 : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 // Asynchronous 16-byte store into another CTA's shared memory; its bytes
 // complete on `cluster_bar`, an mbarrier in the same destination CTA.
 __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint4 v, uint32_t cluster_bar) {
