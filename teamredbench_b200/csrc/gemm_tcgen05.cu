@@ -219,6 +219,29 @@ struct SplitK {
     int group_m;   // m-blocks per raster group (consecutive tiles walk down a group's column)
 };
 
+// One unit of a worker's schedule: a k-block range of a tile.  slot >= 0: the
+// tile is split and this range's fp32 partial goes to workspace slot `slot`
+// (x 2 CTAs of a pair); `contributors` ranges make up the tile.
+struct WorkItem {
+    int tile, kb0, kb1, slot, contributors;
+};
+
+// The idx-th (tile, split) unit of worker `w` out of `P`; false past the last.
+__device__ __forceinline__ bool work_item(int idx, int w, int P, int num_tiles, int num_kb, const SplitK& sk,
+                                          WorkItem& it) {
+    const int unit = w + idx * P;
+    if (unit >= num_tiles * sk.splits) return false;
+    it.tile = unit / sk.splits;
+    it.kb0 = (unit % sk.splits) * sk.kb_per_split;
+    it.kb1 = min(it.kb0 + sk.kb_per_split, num_kb);
+    it.slot = sk.splits > 1 ? unit : -1;
+    it.contributors = sk.splits;
+    return true;
+}
+
+// Workspace slot of the i-th contributor (in K order) of a split tile.
+__device__ __forceinline__ int contributor_slot(int tile, int i, const SplitK& sk) { return tile * sk.splits + i; }
+
 // K order of a unit: with rotate_k, tiles that run at the same time start at
 // different k-blocks, so CTAs sharing one A panel (a single row of tiles,
 // M <= 128) do not all request the same A tile from the same L2 slices at
@@ -444,17 +467,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
                 continue;
             }
-            // ---- split-K: publish this unit's fp32 partial
-            float* wrow = sk.ws + ((size_t)unit * kBM + row_in_tile) * BN;
+            // ---- split-K: publish this unit's fp32 partial.  Workspace blocks are
+            // [16-byte column group][row], row-minor, so a warp's 16-byte stores
+            // (and the fix-up's loads) cover 512 contiguous bytes.
+            uint4* wblk = reinterpret_cast<uint4*>(sk.ws) + (size_t)unit * (BN / 4) * kBM + row_in_tile;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
                 tmem_wait_ld();
                 if (grow < M && nb * BN + c * 32 < N) {
-                    uint4* w4 = reinterpret_cast<uint4*>(wrow + c * 32);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) w4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+                    for (int i = 0; i < 8; ++i)
+                        wblk[(size_t)(c * 8 + i) * kBM] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
                 }
             }
             tc_fence_before();
@@ -469,23 +494,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- last arrival: deterministic sum over splits 0..S-1, convert, store C
             __threadfence();
             if (grow < M) {
-                const float* base = sk.ws + ((size_t)tile * sk.splits * kBM + row_in_tile) * BN;
+                const float4* base =
+                    reinterpret_cast<const float4*>(sk.ws) + (size_t)tile * sk.splits * (BN / 4) * kBM + row_in_tile;
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; ++c) {
                     const int gcol = nb * BN + c * 32;
                     if (gcol >= N) break;
                     float acc_f[32];
-                    const float4* p0 = reinterpret_cast<const float4*>(base + c * 32);
+                    const float4* p0 = base + (size_t)c * 8 * kBM;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float4 v = __ldcg(p0 + i);
+                        const float4 v = __ldcg(p0 + (size_t)i * kBM);
                         acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
                     }
                     for (int sp = 1; sp < sk.splits; ++sp) {
-                        const float4* ps = reinterpret_cast<const float4*>(base + (size_t)sp * kBM * BN + c * 32);
+                        const float4* ps = base + ((size_t)sp * (BN / 4) + c * 8) * kBM;
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const float4 v = __ldcg(ps + i);
+                            const float4 v = __ldcg(ps + (size_t)i * kBM);
                             if constexpr (DT == TRB_INT8) {  // exact integer partial sums
                                 acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
                                 acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
@@ -945,11 +971,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 continue;
             }
-            // ---- split-K: publish this unit's fp32 partial (one TMEM lane = BS words)
+            // ---- split-K: publish this unit's fp32 partial (one TMEM lane = BS words),
+            // lane-minor [16-byte group][lane] so a warp's stores are contiguous
             {
-                uint4* w4 = reinterpret_cast<uint4*>(sk.ws + ((size_t)unit * kBM + n_in_tile) * BS);
+                uint4* w4 = reinterpret_cast<uint4*>(sk.ws) + (size_t)unit * (BS / 4) * kBM + n_in_tile;
 #pragma unroll
-                for (int i = 0; i < BS / 4; ++i) w4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+                for (int i = 0; i < BS / 4; ++i)
+                    w4[(size_t)i * kBM] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
             }
             __threadfence();
             named_barrier(1, 128);
@@ -959,19 +987,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!last_split_flag) continue;
             __threadfence();
             if (gn < N) {
-                const float* base = sk.ws + ((size_t)tile * sk.splits * kBM + n_in_tile) * BS;
+                const float4* base =
+                    reinterpret_cast<const float4*>(sk.ws) + (size_t)tile * sk.splits * (BS / 4) * kBM + n_in_tile;
                 float acc_f[BS];
-                const float4* p0 = reinterpret_cast<const float4*>(base);
 #pragma unroll
                 for (int i = 0; i < BS / 4; ++i) {
-                    const float4 v = __ldcg(p0 + i);
+                    const float4 v = __ldcg(base + (size_t)i * kBM);
                     acc_f[4 * i] = v.x; acc_f[4 * i + 1] = v.y; acc_f[4 * i + 2] = v.z; acc_f[4 * i + 3] = v.w;
                 }
                 for (int sp = 1; sp < sk.splits; ++sp) {
-                    const float4* ps = reinterpret_cast<const float4*>(base + (size_t)sp * kBM * BS);
+                    const float4* ps = base + (size_t)sp * (BS / 4) * kBM;
 #pragma unroll
                     for (int i = 0; i < BS / 4; ++i) {
-                        const float4 v = __ldcg(ps + i);
+                        const float4 v = __ldcg(ps + (size_t)i * kBM);
                         if constexpr (DT == TRB_INT8) {
                             acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
                             acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
@@ -1067,7 +1095,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int num_n = (N + kPairN - 1) / kPairN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + kBKElems - 1) / kBKElems;
-    const int num_units = num_tiles * sk.splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPairStages; ++s) {
@@ -1102,11 +1129,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;
             bool ok = true;
-            for (int unit = pair; ok && unit < num_units; unit += num_pairs) {
+            WorkItem it;
+            for (int idx = 0; ok && work_item(idx, pair, num_pairs, num_tiles, num_kb, sk, it); ++idx) {
                 int mb, nb;
-                tile_coords(unit / sk.splits, num_m, num_n, sk.group_m, mb, nb);
-                const int kb0 = (unit % sk.splits) * sk.kb_per_split;
-                const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
+                tile_coords(it.tile, num_m, num_n, sk.group_m, mb, nb);
+                const int kb0 = it.kb0, kb1 = it.kb1;
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait_cluster(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrProducerWait);
@@ -1151,9 +1178,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, phase = 0;
             bool ok = true;
             int t_local = 0;
-            for (int unit = pair; ok && unit < num_units; unit += num_pairs, ++t_local) {
-                const int kb0 = (unit % sk.splits) * sk.kb_per_split;
-                const int kb1 = min(kb0 + sk.kb_per_split, num_kb);
+            WorkItem it;
+            for (int idx = 0; ok && work_item(idx, pair, num_pairs, num_tiles, num_kb, sk, it); ++idx, ++t_local) {
+                const int kb0 = it.kb0, kb1 = it.kb1;
                 const int acc = t_local & 1;
                 const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
                 if (!mbar_wait_cluster(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
@@ -1197,15 +1224,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t acce_leader0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
         const uint32_t acce_leader1 = mapa_shared(smem_u32(&acce_bar[1]), 0);
         int t_local = 0;
-        for (int unit = pair; unit < num_units; unit += num_pairs, ++t_local) {
-            const int tile = unit / sk.splits;
+        WorkItem it;
+        for (int idx = 0; work_item(idx, pair, num_pairs, num_tiles, num_kb, sk, it); ++idx, ++t_local) {
+            const int tile = it.tile;
             int mb, nb;
             tile_coords(tile, num_m, num_n, sk.group_m, mb, nb);
             const int acc = t_local & 1;
             const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
             bool ok = mbar_wait_cluster(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
             ok = __all_sync(0xffffffffu, ok);
-            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);
+            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);  // the fix-up below is CTA-wide
             if (!ok) {
                 if (lane == 0) {
                     atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
@@ -1217,7 +1245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int grow = mb * kPairM + (int)rank * kBM + row_in_tile;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kPairN);
             const uint32_t acce_remote = acc ? acce_leader1 : acce_leader0;
-            if (sk.splits == 1) {
+            if (it.slot < 0) {
 #pragma unroll 1
                 for (int c = 0; c < kPairN / 32; ++c) {
                     uint32_t r[32];
@@ -1231,18 +1259,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive_cluster(acce_remote);
                 continue;
             }
-            // ---- split-K: slot (unit, rank) holds this CTA's 128-row partial
-            const size_t slot = (size_t)unit * 2 + rank;
-            float* wrow = sk.ws + (slot * kBM + row_in_tile) * kPairN;
+            // ---- split tile: slot (it.slot, rank) holds this CTA's 128-row partial
+            // (blocks [16-byte column group][row], row-minor: a warp's stores are contiguous)
+            const size_t slot = (size_t)it.slot * 2 + rank;
+            uint4* wblk = reinterpret_cast<uint4*>(sk.ws) + slot * (kPairN / 4) * kBM + row_in_tile;
 #pragma unroll 1
             for (int c = 0; c < kPairN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
                 tmem_wait_ld();
                 if (grow < M && nb * kPairN + c * 32 < N) {
-                    uint4* w4 = reinterpret_cast<uint4*>(wrow + c * 32);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) w4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+                    for (int i = 0; i < 8; ++i)
+                        wblk[(size_t)(c * 8 + i) * kBM] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
                 }
             }
             tc_fence_before();
@@ -1252,7 +1281,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             named_barrier(1, 128);
             const size_t counter = (size_t)tile * 2 + rank;
             if (first_epi_thread)
-                last_split_flag = atomicAdd(&sk.counters[counter], 1u) == (unsigned)(sk.splits - 1);
+                last_split_flag = atomicAdd(&sk.counters[counter], 1u) == (unsigned)(it.contributors - 1);
             named_barrier(1, 128);
             if (!last_split_flag) continue;
             __threadfence();
@@ -1264,13 +1293,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     float acc_f[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) acc_f[i] = 0.0f;
-                    for (int sp = 0; sp < sk.splits; ++sp) {
-                        const size_t sslot = ((size_t)tile * sk.splits + sp) * 2 + rank;
-                        const float4* ps = reinterpret_cast<const float4*>(
-                            sk.ws + (sslot * kBM + row_in_tile) * kPairN + c * 32);
+                    for (int sp = 0; sp < it.contributors; ++sp) {  // K order
+                        const size_t sslot = (size_t)contributor_slot(tile, sp, sk) * 2 + rank;
+                        const float4* ps = reinterpret_cast<const float4*>(sk.ws) +
+                                           (sslot * (kPairN / 4) + (size_t)c * 8) * kBM + row_in_tile;
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const float4 v = __ldcg(ps + i);
+                            const float4 v = __ldcg(ps + (size_t)i * kBM);
                             if constexpr (DT == TRB_INT8) {
                                 acc_f[4 * i] = __int_as_float(__float_as_int(acc_f[4 * i]) + __float_as_int(v.x));
                                 acc_f[4 * i + 1] = __int_as_float(__float_as_int(acc_f[4 * i + 1]) + __float_as_int(v.y));
@@ -1633,7 +1662,7 @@ static int launch_swap(const void* a, const void* b, int m, int n, int k, void* 
     // No K rotation: the S box is only BS x 128 bytes, and CTAs that walk K in
     // step read whole rows of B together (measured 29.1 vs 30.7 us at
     // M = 16, N = K = 8192 bf16 with per-tile rotation).
-    SplitK sk{1, num_kb, nullptr, nullptr, 0};
+    SplitK sk{1, num_kb, nullptr, nullptr, 0, 0};
     int grid;
     if constexpr (CL > 1) {
         sk.splits = CL;
@@ -1838,6 +1867,9 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     const int kbps = (num_kb + splits - 1) / splits;
     splits = (num_kb + kbps - 1) / kbps;
     SplitK sk{splits, kbps, nullptr, nullptr, 0, raster_group(kPairM, k, es)};
+    // (A stream-K tail -- the last partial wave's tiles spread over all pairs in
+    // equal k-block ranges -- measured 15-45% slower than whole tiles at 4096^3
+    // and 3072 x 4096 x 2048 on B200, and was dropped.)
     if (splits > 1) {
         rc = ensure_workspace(dev, (size_t)tiles * splits * 2 * kBM * kPairN * sizeof(float), (size_t)tiles * 2, &sk);
         if (rc != TRB_OK) return rc;
@@ -1849,7 +1881,14 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
                    out_scale, sk);
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaGetLastError());
-    if (info) *info = {grid_workers * 2, kThreads, splits, 1, kPairN};
+    if (info) {
+        *info = LaunchInfo{};
+        info->grid = grid_workers * 2;
+        info->block = kThreads;
+        info->splits = splits;
+        info->pair = 1;
+        info->tile_n = kPairN;
+    }
     return TRB_OK;
 }
 
@@ -2067,7 +2106,7 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)TileCfg<256>::kSmem));
-    SplitK sk{splits, kbps, nullptr, nullptr, 0};
+    SplitK sk{splits, kbps, nullptr, nullptr, 0, 0};
     if (splits > 1) {
         // The array keeps the previous call's contents: counters must start at zero.
         TRB_CUDA(cudaMemsetAsync(scratch.counters, 0, counter_bytes, stream));

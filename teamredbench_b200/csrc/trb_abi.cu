@@ -343,7 +343,8 @@ static void gemm_impl_name(const gemm::LaunchInfo& info, char* out, size_t size,
     snprintf(out, size, "%stcgen05_%s_%dx%d%s%s", info.fp32x3 ? "fp32x3_" : "",
              info.pair ? "cta_pair" : info.swap ? "swap" : "1cta", info.pair ? 256 : 128, info.tile_n,
              info.cluster > 1 ? (info.cluster == 2 ? "_cluster2" : info.cluster == 4 ? "_cluster4" : "_cluster8")
-                              : info.splits > 1 ? "_splitk" : "",
+             : info.splits > 1 ? "_splitk"
+                              : "",
              suffix);
 }
 
