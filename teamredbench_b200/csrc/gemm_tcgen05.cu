@@ -49,7 +49,6 @@ constexpr int kBStage = kBN * kBKBytes;  // 32 KiB
 constexpr int kNumAcc = 2;
 constexpr int kTmemCols = kNumAcc * kBN;  // 512
 constexpr int kThreads = 192;
-constexpr size_t kSmemBytes = (size_t)kStages * (kAStage + kBStage) + 1024;  // + alignment slack
 
 // Single-CTA tile-width variants: BN = 256 (default), 128 and 64 (skinny
 // problems: M <= 128 gives one row of tiles, so a narrow N tile is what puts
