@@ -25,9 +25,6 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
-# The contract is one JSON line on stdout; NCCL's own log lines (its version
-# banner when NCCL_DEBUG is set in the environment) go to stderr instead.
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
@@ -191,7 +188,22 @@ def run_b200(args) -> None:
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # NCCL may print its version banner on stdout when its communicator
+        # comes up (depending on the environment's NCCL settings); the
+        # contract is one JSON line there, so fd 1 points at stderr until the
+        # first collective has created the communicator.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+            warm = torch.zeros(1, device=torch.device("cuda", local))
+            dist.all_reduce(warm)
+            torch.cuda.synchronize(local)
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
     dev = torch.device("cuda", local)
 
     def barrier():
