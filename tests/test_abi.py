@@ -33,9 +33,10 @@ def test_library_loads_and_exports_every_symbol():
 def test_struct_layout_matches_c(tmp_path: Path):
     probe = tmp_path / "probe.c"
     probe.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "trb_b200.h"\n'
-                     'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(trb_result), '
+                     'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(trb_result), '
                      'offsetof(trb_result, implementation), sizeof(trb_hbm_args), offsetof(trb_hbm_args, scale), '
-                     'sizeof(trb_gemm_args), offsetof(trb_result, launches)); return 0;}\n')
+                     'sizeof(trb_gemm_args), offsetof(trb_result, launches), sizeof(trb_gemm_options), '
+                     'offsetof(trb_gemm_options, b_layout), offsetof(trb_gemm_options, tile_n)); return 0;}\n')
     exe = tmp_path / "probe"
     subprocess.run(["gcc", f"-I{ROOT / 'include'}", str(probe), "-o", str(exe)], check=True)
     got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
@@ -43,7 +44,8 @@ def test_struct_layout_matches_c(tmp_path: Path):
 
     assert got == [ctypes.sizeof(_native.TrbResult), _native.TrbResult.implementation.offset,
                    ctypes.sizeof(_native.HbmArgs), _native.HbmArgs.scale.offset, ctypes.sizeof(_native.GemmArgs),
-                   _native.TrbResult.launches.offset]
+                   _native.TrbResult.launches.offset, ctypes.sizeof(_native.GemmOptions),
+                   _native.GemmOptions.b_layout.offset, _native.GemmOptions.tile_n.offset]
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
