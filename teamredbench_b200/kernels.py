@@ -21,19 +21,34 @@ _TORCH_TO_TRB = {
 }
 
 
+_DTYPE_CACHE: dict[Any, str] = {}  # torch.dtype object -> library dtype name, filled on first use
+
+
 def trb_dtype(tensor: Any) -> str:
-    name = _TORCH_TO_TRB.get(str(tensor.dtype))
+    name = _DTYPE_CACHE.get(tensor.dtype)
     if name is None:
-        raise _native.NativeSkipped(1, f"unsupported tensor dtype {tensor.dtype}")
+        name = _TORCH_TO_TRB.get(str(tensor.dtype))
+        if name is None:
+            raise _native.NativeSkipped(1, f"unsupported tensor dtype {tensor.dtype}")
+        _DTYPE_CACHE[tensor.dtype] = name
     return name
 
 
 def _stream_handle(tensor: Any, stream: Any | None) -> int:
+    """Raw cudaStream_t of ``stream``, or of the device's current stream.
+
+    The current stream is read through torch's raw-handle query (one C call,
+    no Stream object built), which keeps the per-call host cost of a small
+    GEMM close to the bare ctypes call; torch builds without it take the
+    public ``torch.cuda.current_stream``."""
     import torch
 
-    if stream is None:
-        stream = torch.cuda.current_stream(tensor.device)
-    return int(stream.cuda_stream)
+    if stream is not None:
+        return int(stream.cuda_stream)
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return int(raw(tensor.get_device()))
+    return int(torch.cuda.current_stream(tensor.device).cuda_stream)
 
 
 def _require_cuda_contiguous(*tensors: Any) -> None:
@@ -82,12 +97,13 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     swapped-operand skinny kernel (C^T = B^T A^T, m <= 64; automatic for
     m <= 64)."""
     _require_cuda_contiguous(a, b, out)
-    bk, bn = (b.shape[1], b.shape[0]) if b_transposed else (b.shape[0], b.shape[1])
-    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != bk:
-        raise ValueError(f"incompatible shapes {tuple(a.shape)} x {tuple(b.shape)} (b_transposed={b_transposed})")
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError(f"gemm operands must be 2-D, got {tuple(a.shape)} x {tuple(b.shape)}")
     m, k = a.shape
-    n = bn
-    if tuple(out.shape) != (m, n):
+    n, bk = b.shape if b_transposed else reversed(b.shape)
+    if bk != k:
+        raise ValueError(f"incompatible shapes {tuple(a.shape)} x {tuple(b.shape)} (b_transposed={b_transposed})")
+    if out.shape != (m, n):
         raise ValueError(f"out must be {(m, n)}, got {tuple(out.shape)}")
     name = dtype or trb_dtype(a)
     _native.gemm_launch_ex(name, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), float(scale_a),
