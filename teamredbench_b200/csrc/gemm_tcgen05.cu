@@ -54,11 +54,27 @@ constexpr int kThreads = 192;
 // problems: M <= 128 gives one row of tiles, so a narrow N tile is what puts
 // every SM to work).  The ring is as deep as the 227 KiB of shared memory
 // allows; TMEM holds two BN-column accumulators.
-template <int BN>
+// KD k-blocks share one ring stage (one full/empty barrier round trip).  A
+// one-k-block stage of a 64- or 128-wide tile holds only 4 MMAs' worth of
+// work (~140 ns), less than the MMA thread's per-stage cost on B200 (~260 ns
+// measured with a 4-MMA stage), so the 128-wide ring takes 2 k-blocks per
+// stage (3 stages) and the 64-wide ring 4 (2 stages): 1024^3 bf16 went from
+// 6.9 to 6.0 (2 per stage) and 5.8 us (4 per stage).  Cluster split-K runs
+// (one row of tiles, an HBM stream of B) keep the deeper one-k-block ring
+// for 16- and 32-bit types, where the MMAs keep up with HBM anyway (M = 128,
+// N = K = 8192: 28.1 us against 28.7 with 2 per stage); 8-bit types, whose
+// k-blocks carry twice the K, take 2 per stage there (13.7 against 14.4 us).
+__host__ __device__ constexpr int tile_kd(int bn, int cl, int es) {
+    return bn == 256 ? 1 : cl > 1 ? (es == 1 ? 2 : 1) : (bn == 64 ? 4 : 2);
+}
+
+template <int BN, int KD>
 struct TileCfg {
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
-    static constexpr int kBStage = BN * kBKBytes;
-    static constexpr int kStageBytes = kAStage + kBStage;
+    static_assert(KD == 1 || KD == 2 || KD == 4, "k-blocks per stage");
+    static constexpr int kKD = KD;
+    static constexpr int kBStage = BN * kBKBytes;  // one k-block of B
+    static constexpr int kStageBytes = kKD * (kAStage + kBStage);
     static constexpr int kStages = (210 * 1024) / kStageBytes > 8 ? 8 : (210 * 1024) / kStageBytes;
     static constexpr int kTmemCols = kNumAcc * BN;
     static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
@@ -270,13 +286,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kBBoxes = BN / kBoxN;                    // B boxes per stage
     constexpr int kBBoxBytes = kBKElems * 128;              // bytes of one B box == MN-atom stride (LBO)
     constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;  // K rows of B per instruction
-    using Cfg = TileCfg<BN>;
+    using Cfg = TileCfg<BN, tile_kd(BN, CL, Tr::kEsize)>;
     constexpr int kStagesT = Cfg::kStages;
-    constexpr int kBStageT = Cfg::kBStage;
+    constexpr int kKD = Cfg::kKD;                   // k-blocks per stage
+    constexpr int kBStageT = Cfg::kBStage;          // B bytes of one k-block
+    constexpr int kAStageKD = kKD * kAStage;        // A bytes of one stage
+    constexpr int kBStageKD = kKD * kBStageT;       // B bytes of one stage
     constexpr uint32_t kIdesc1 = idesc_with_n(KB ? idesc_b_kmajor(Tr::kIdesc) : Tr::kIdesc, BN);
     static_assert(KB || BN >= kBoxN, "MN-major B needs at least one 128-byte swizzle row per tile");
     static_assert(CL == 1 || ((CL == 2 || CL == 4 || CL == 8) && (BN / CL) % 32 == 0), "cluster split");
-    static_assert(CL == 1 || (size_t)kBM * BN * 4 <= (size_t)kStagesT * (kAStage + kBStageT), "receive buffer");
+    static_assert(CL == 1 || (size_t)kBM * BN * 4 <= (size_t)kStagesT * (kAStageKD + kBStageKD), "receive buffer");
+    static_assert((size_t)kStagesT * (kAStageKD + kBStageKD) + 1024 == Cfg::kSmem, "ring footprint");
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kStagesT];
@@ -291,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = smem_base;
-    const uint32_t sB = smem_base + kStagesT * kAStage;
+    const uint32_t sB = smem_base + kStagesT * kAStageKD;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -342,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
                 const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
                 const int rot = k_rotation(sk, unit / sk.splits, nk);
-                for (int i = 0; i < nk; ++i) {
-                    const int kb = kb0 + (i + rot < nk ? i + rot : i + rot - nk);
+                for (int i0 = 0; i0 < nk; i0 += kKD) {  // one stage: k-blocks i0 .. i0 + cnt - 1
+                    const int cnt = min(kKD, nk - i0);
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrProducerWait);
                         abort_flag = 1;
@@ -351,15 +371,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
-                    mbar_arrive_expect_tx(fb, kAStage + kBStageT);
-                    tma_load_2d(sA + stage * kAStage, &tmA, fb, kb * kBKElems, mb * kBM);
-                    if constexpr (KB) {
-                        tma_load_2d(sB + stage * kBStageT, &tmB, fb, kb * kBKElems, nb * BN);
-                    } else {
+                    mbar_arrive_expect_tx(fb, (uint32_t)cnt * (kAStage + kBStageT));
 #pragma unroll
-                        for (int j = 0; j < kBBoxes; ++j)
-                            tma_load_2d(sB + stage * kBStageT + j * kBBoxBytes, &tmB, fb, nb * BN + j * kBoxN,
-                                        kb * kBKElems);
+                    for (int d = 0; d < kKD; ++d) {
+                        if (d >= cnt) break;
+                        const int i = i0 + d;
+                        const int kb = kb0 + (i + rot < nk ? i + rot : i + rot - nk);
+                        const uint32_t a_dst = sA + stage * kAStageKD + d * kAStage;
+                        const uint32_t b_dst = sB + stage * kBStageKD + d * kBStageT;
+                        tma_load_2d(a_dst, &tmA, fb, kb * kBKElems, mb * kBM);
+                        if constexpr (KB) {
+                            tma_load_2d(b_dst, &tmB, fb, kb * kBKElems, nb * BN);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < kBBoxes; ++j)
+                                tma_load_2d(b_dst + j * kBBoxBytes, &tmB, fb, nb * BN + j * kBoxN, kb * kBKElems);
+                        }
                     }
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
@@ -398,7 +425,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                for (int i = 0; i < nk; ++i) {  // same (rotated) order as the producer; only the count matters here
+                for (int i0 = 0; i0 < nk; i0 += kKD) {  // same stages as the producer; only the counts matter here
+                    const int cnt = min(kKD, nk - i0);
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
@@ -406,14 +434,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     // TMA completion is ordered before the MMA by the barrier's
-                    // transaction count: no tcgen05 fence is needed per k-block.
-                    const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kAStage) >> 4);
-                    const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kBStageT) >> 4);
+                    // transaction count: no tcgen05 fence is needed per stage.
+                    const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kAStageKD) >> 4);
+                    const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kBStageKD) >> 4);
 #pragma unroll
-                    for (int ks = 0; ks < kKSteps; ++ks)
-                        mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kInstrKBytes >> 4),
-                                       b_stage + (uint64_t)(ks * kBKStep >> 4), kIdesc1,
-                                       (i != 0 || ks != 0) ? 1u : 0u);
+                    for (int d = 0; d < kKD; ++d) {
+                        if (d >= cnt) break;
+#pragma unroll
+                        for (int ks = 0; ks < kKSteps; ++ks)
+                            mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)((d * kAStage + ks * kInstrKBytes) >> 4),
+                                           b_stage + (uint64_t)((d * kBStageT + ks * kBKStep) >> 4), kIdesc1,
+                                           (i0 != 0 || d != 0 || ks != 0) ? 1u : 0u);
+                    }
                     tc_commit(smem_u32(&empty_bar[stage]));  // frees the smem stage when these MMAs finish
                     if (++stage == kStagesT) {
                         stage = 0;
@@ -1478,9 +1510,12 @@ static KernelChoice choose_kernel(int m, int n, int num_kb, bool allow_bn64, int
         const bool one_wave = tiles <= sms / 2;
         best_score = wave_eff(tiles, sms / 2) * (one_wave && num_kb < 40 ? 0.85 : 1.0);
     }
+    // Per-tile efficiency of the single-CTA widths relative to the CTA pair,
+    // from full-wave runs at 4096^3 bf16 (105 / 120 / 177 us for 256 / 128 /
+    // 64 wide; the 64- and 128-wide rings take 4 and 2 k-blocks per stage).
     for (int bn : {256, 128, 64}) {
         if (bn == 64 && !allow_bn64) continue;
-        const double f = bn == 256 ? 0.89 : bn == 128 ? 0.72 : 0.50;
+        const double f = bn == 256 ? 0.89 : bn == 128 ? 0.78 : 0.53;
         const double score = wave_eff(mb * ((n + bn - 1) / bn), sms) * f;
         if (score > best_score + 1e-9) {
             best_score = score;
@@ -1545,7 +1580,7 @@ template <int DT, bool KB, int BN, int CL = 1>
 static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, int n, int k, void* c,
                          float out_scale, int splits, int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
     using Tr = Traits<DT>;
-    using Cfg = TileCfg<BN>;
+    using Cfg = TileCfg<BN, tile_kd(BN, CL, Tr::kEsize)>;
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {
         TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, KB, BN, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1813,9 +1848,9 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         tile_n_single = bn;
     } else if (splits == 0 && cta_pair < 0 && tile_n_opt == 0) {
         auto capacity = [dev](int c) {
-            return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfg<256>::kSmem, dev, 2)
-                   : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfg<256>::kSmem, dev, 4)
-                            : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfg<256>::kSmem, dev, 8);
+            return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfg<256, 1>::kSmem, dev, 2)
+                   : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfg<256, 1>::kSmem, dev, 4)
+                            : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfg<256, 1>::kSmem, dev, 8);
         };
         const KernelChoice kc = choose_kernel(m, n, num_kb, KB || es >= 2, sms, capacity);
         pair_auto = kc.pair;
@@ -2104,7 +2139,7 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)TileCfg<256>::kSmem));
+                                  (int)TileCfg<256, 1>::kSmem));
     SplitK sk{splits, kbps, nullptr, nullptr, 0, 0};
     if (splits > 1) {
         // The array keeps the previous call's contents: counters must start at zero.
@@ -2114,7 +2149,7 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     }
     const long units = tiles * splits;
     const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
-    gemm_tcgen05_kernel<DT, false, 256><<<grid, kThreads, TileCfg<256>::kSmem, stream>>>(tmA, tmB, c, m, n, k,
+    gemm_tcgen05_kernel<DT, false, 256><<<grid, kThreads, TileCfg<256, 1>::kSmem, stream>>>(tmA, tmB, c, m, n, k,
                                                                                          out_scale, sk);
     TRB_CUDA(cudaGetLastError());
     return TRB_OK;
