@@ -163,7 +163,7 @@ int main(int argc, char** argv) {
     std::printf("{\"status\":\"ok\",\"raw_metrics\":{\"elapsed_s\":%.9e,\"achieved_ops\":%.0f},\"metadata\":{",
                 r.elapsed_s, r.achieved_ops);
     print_common_metadata(r);
-    std::printf(",\"k_stage_bytes\":128,\"split_k\":%d,\"b_layout\":\"%s\"}}\n", r.split_k, b_layout.c_str());
+    std::printf(",\"k_block_bytes\":128,\"split_k\":%d,\"b_layout\":\"%s\"}}\n", r.split_k, b_layout.c_str());
 #endif
     std::fflush(stdout);
     return 0;
