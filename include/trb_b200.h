@@ -169,7 +169,9 @@ int trb_hbm_host(int dtype, int mode, void* dst_host, const void* src_host, cons
 /* ---- dense GEMM (tcgen05 / TMEM / TMA) ---------------------------------- */
 
 /* Allocate A (m x k), B (k x n), C (m x n), fill with seeded values in the
- * BASELINE distributions, time `iterations` launches.  Replaces
+ * BASELINE distributions, time `iterations` launches (after a warm-up they are
+ * replayed from a CUDA graph captured once, so host launch work does not
+ * enter the device-timed loop).  Replaces
  * run_low_precision_kernel / run_high_precision_kernel of the reference's
  * mfu_hipblas executable (src/teamredbench/native/kernels/mfu_gemm_lowp.hip.hpp:
  * 343-486, mfu_gemm_highp.hip.hpp:228-336) and its dispatch
