@@ -9,11 +9,13 @@
 // one instruction and one operand fetch per 8 FMAs per lane).
 //  * 256 threads per CTA compute a 128 x 128 tile; 8 warps in a 2 (M) x 4 (N)
 //    grid, each warp 64 x 32 = 8 x 4 DMMA tiles, 64 fp64 accumulators per lane;
-//  * K advances 16 at a time through a 4-stage cp.async ring (16-byte copies
-//    when the rows are 16-byte multiples and the pointers aligned, else 8-byte);
+//  * K advances 32 at a time through a 3-stage cp.async ring (216 KiB; 16-byte
+//    copies when the rows are 16-byte multiples and the pointers aligned, else
+//    8-byte).  One CTA barrier per 32 K instead of per 16 measured 32.6 against
+//    31.6 TFLOP/s at 8192^3;
 //    out-of-range elements are zero-filled by the copy (src-size 0), and
 //    out-of-range outputs are not stored, so any M, N, K works;
-//  * A and B^T tiles are stored [row][16 + 4] doubles, row-major B tiles
+//  * A and B^T tiles are stored [row][32 + 4] doubles, row-major B tiles
 //    [k][128 + 8]: the padding puts the 8 x 4 fragment of a warp's load in the
 //    minimum two shared-memory wavefronts;
 //  * either B layout: row-major K x N, or B^T stored N x K (K-major).
@@ -25,9 +27,9 @@ namespace trb {
 namespace dgemm {
 
 constexpr int kTile = 128;
-constexpr int kBK = 16;
+constexpr int kBK = 32;
 constexpr int kThreads = 256;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kKPad = kBK + 4;      // doubles per row of a k-contiguous tile
 constexpr int kNPad = kTile + 8;    // doubles per k-row of an n-contiguous tile
 constexpr int kTileKc = kTile * kKPad;  // k-contiguous tile, doubles
@@ -54,7 +56,7 @@ __device__ __forceinline__ void dmma(double& d0, double& d1, double a, double b)
                  : "d"(a), "d"(b));
 }
 
-// Copy a 128-row x 16-double tile of a k-contiguous matrix (rows of length K,
+// Copy a 128-row x kBK-double tile of a k-contiguous matrix (rows of length K,
 // leading dimension K) into smem [row][kKPad].  V = doubles per copy (2 or 1).
 template <int V>
 __device__ __forceinline__ void load_kc(uint32_t dst, const double* __restrict__ src, int row0, int rows, int k0,
@@ -72,7 +74,7 @@ __device__ __forceinline__ void load_kc(uint32_t dst, const double* __restrict__
     }
 }
 
-// Copy a 16-k-row x 128-column tile of a row-major K x N matrix into smem [k][kNPad].
+// Copy a kBK-k-row x 128-column tile of a row-major K x N matrix into smem [k][kNPad].
 template <int V>
 __device__ __forceinline__ void load_nc(uint32_t dst, const double* __restrict__ src, int k0, int K, int n0, int N) {
     constexpr int kChunks = kBK * kTile / V;
