@@ -68,16 +68,17 @@ __host__ __device__ constexpr int tile_kd(int bn, int cl, int es) {
     return bn == 256 ? 1 : cl > 1 ? (es == 1 ? 2 : 1) : (bn == 64 ? 4 : 2);
 }
 
-template <int BN, int KD>
+template <int BN, int KD, int EPI>
 struct TileCfg {
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
     static_assert(KD == 1 || KD == 2 || KD == 4, "k-blocks per stage");
     static constexpr int kKD = KD;
+    static constexpr int kEpiBytes = EPI;  // TMA-store staging after the ring
     static constexpr int kBStage = BN * kBKBytes;  // one k-block of B
     static constexpr int kStageBytes = kKD * (kAStage + kBStage);
     static constexpr int kStages = (210 * 1024) / kStageBytes > 8 ? 8 : (210 * 1024) / kStageBytes;
     static constexpr int kTmemCols = kNumAcc * BN;
-    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + EPI;
 };
 
 // Instruction descriptor (kind::f16 / tf32 / f8f6f4 / i8): D format, A/B formats,
@@ -172,29 +173,43 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     nb = local / gm;
 }
 
+// Output element bytes: bf16 for bf16 / e4m3 inputs, f16 for f16, f32 for
+// tf32, s32 for int8.
+template <int DT>
+__host__ __device__ constexpr int out_esize() {
+    return (DT == TRB_TFLOAT32 || DT == TRB_INT8) ? 4 : 2;
+}
+
+// 32 fp32 accumulator words of one row -> 16 words of packed bf16 / f16 pairs
+// (e4m3 results scaled by out_scale first).
+template <int DT>
+__device__ __forceinline__ void convert16(const uint32_t (&r)[32], float out_scale, uint32_t (&w)[16]) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float lo = __uint_as_float(r[2 * i]), hi = __uint_as_float(r[2 * i + 1]);
+        if constexpr (DT == TRB_FLOAT8_E4M3FN) {
+            lo *= out_scale;
+            hi *= out_scale;
+        }
+        if constexpr (DT == TRB_FLOAT16) {
+            __half2 h = __floats2half2_rn(lo, hi);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+            __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+    }
+}
+
 // Convert 32 accumulator words of one row and store them at C[row, col .. col+31].
 template <int DT>
 __device__ __forceinline__ void store_chunk(void* C, int row, int col, int N, const uint32_t (&r)[32],
                                             float out_scale) {
     const bool full = col + 32 <= N;
-    if constexpr (DT == TRB_BFLOAT16 || DT == TRB_FLOAT8_E4M3FN || DT == TRB_FLOAT16) {
+    if constexpr (out_esize<DT>() == 2) {
         uint16_t* out = static_cast<uint16_t*>(C) + (size_t)row * N + col;
         uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            float lo = __uint_as_float(r[2 * i]), hi = __uint_as_float(r[2 * i + 1]);
-            if constexpr (DT == TRB_FLOAT8_E4M3FN) {
-                lo *= out_scale;
-                hi *= out_scale;
-            }
-            if constexpr (DT == TRB_FLOAT16) {
-                __half2 h = __floats2half2_rn(lo, hi);
-                w[i] = *reinterpret_cast<uint32_t*>(&h);
-            } else {
-                __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-                w[i] = *reinterpret_cast<uint32_t*>(&h);
-            }
-        }
+        convert16<DT>(r, out_scale, w);
         if (full) {
             uint4* o4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
@@ -215,6 +230,54 @@ __device__ __forceinline__ void store_chunk(void* C, int row, int col, int N, co
             for (int i = 0; i < 32; ++i)
                 if (col + i < N) out[i] = r[i];
         }
+    }
+}
+
+// TMA-store epilogue of whole (unsplit) tiles.  Each epilogue warp owns 32
+// TMEM lanes (rows) and writes its rows 32 columns at a time: convert, place
+// the 32 x 32 box in shared memory in the C tensor map's swizzle, and one lane
+// stores it with cp.async.bulk.tensor, which writes whole sectors and lets the
+// warp go on to the next box (two staging buffers per warp).  Rows or columns
+// past M / N are clipped by the store.  Stores of 16 bytes per row per lane
+// straight from registers cost 11-13% of a 128 x 256 tile's time at 2048^3 and
+// 4096^3 bf16 (measured by dropping them).
+template <int DT>
+__host__ __device__ constexpr int epi_box_bytes() {
+    return 32 * 32 * out_esize<DT>();
+}
+template <int DT>
+__host__ __device__ constexpr int epi_bytes() {
+    return 4 * 2 * epi_box_bytes<DT>();  // 4 epilogue warps x 2 buffers
+}
+
+// Shared-memory plan of gemm_tcgen05_kernel<DT, *, BN, CL>.  Cluster split-K
+// runs store through the exchange path and need no staging; 64-wide tiles
+// keep direct stores (two boxes per warp per tile, where waiting for the
+// last store before exit outweighs the gain: 1024^3 bf16 5.78 against 5.69 us).
+template <int DT, int BN, int CL>
+using TileCfgFor = TileCfg<BN, tile_kd(BN, CL, Traits<DT>::kEsize), (CL == 1 && BN >= 128) ? epi_bytes<DT>() : 0>;
+
+// Row `row` (0..31) of a staging box at `buf` (1 KiB aligned): 16-bit outputs
+// are 64-byte rows in the 64-byte swizzle (16-byte chunk j at j ^ ((row >> 1) & 3)),
+// 32-bit outputs 128-byte rows in the 128-byte swizzle (chunk j at j ^ (row & 7)),
+// the layouts CU_TENSOR_MAP_SWIZZLE_64B / _128B read.  A warp's stores of one
+// chunk index then fill whole shared-memory wavefronts.
+template <int DT>
+__device__ __forceinline__ void stage_row(uint32_t buf, int row, const uint32_t (&r)[32], float out_scale) {
+    if constexpr (out_esize<DT>() == 2) {
+        uint32_t w[16];
+        convert16<DT>(r, out_scale, w);
+        const uint32_t base = buf + (uint32_t)(row * 64);
+        const int sw = (row >> 1) & 3;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            st_shared_v4(base + (uint32_t)((j ^ sw) * 16), w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    } else {  // tf32 -> f32, int8 -> s32: raw 32-bit words
+        const uint32_t base = buf + (uint32_t)(row * 128);
+        const int sw = row & 7;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            st_shared_v4(base + (uint32_t)((j ^ sw) * 16), r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
     }
 }
 
@@ -279,14 +342,15 @@ __device__ __forceinline__ int k_rotation(const SplitK& sk, int tile, int nk) {
 template <int DT, bool KB, int BN, int CL = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
+                        const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K,
+                        float out_scale, SplitK sk) {
     using Tr = Traits<DT>;
     constexpr int kBKElems = kBKBytes / Tr::kEsize;         // K elements per stage
     constexpr int kBoxN = 128 / Tr::kEsize;                 // N elements per B box (one swizzle row)
     constexpr int kBBoxes = BN / kBoxN;                    // B boxes per stage
     constexpr int kBBoxBytes = kBKElems * 128;              // bytes of one B box == MN-atom stride (LBO)
     constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;  // K rows of B per instruction
-    using Cfg = TileCfg<BN, tile_kd(BN, CL, Tr::kEsize)>;
+    using Cfg = TileCfgFor<DT, BN, CL>;
     constexpr int kStagesT = Cfg::kStages;
     constexpr int kKD = Cfg::kKD;                   // k-blocks per stage
     constexpr int kBStageT = Cfg::kBStage;          // B bytes of one k-block
@@ -296,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     static_assert(KB || BN >= kBoxN, "MN-major B needs at least one 128-byte swizzle row per tile");
     static_assert(CL == 1 || ((CL == 2 || CL == 4 || CL == 8) && (BN / CL) % 32 == 0), "cluster split");
     static_assert(CL == 1 || (size_t)kBM * BN * 4 <= (size_t)kStagesT * (kAStageKD + kBStageKD), "receive buffer");
-    static_assert((size_t)kStagesT * (kAStageKD + kBStageKD) + 1024 == Cfg::kSmem, "ring footprint");
+    static_assert((size_t)kStagesT * (kAStageKD + kBStageKD) + 1024 + Cfg::kEpiBytes == Cfg::kSmem, "footprint");
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kStagesT];
@@ -312,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = smem_base;
     const uint32_t sB = smem_base + kStagesT * kAStageKD;
+    const uint32_t sEpi = sB + kStagesT * kBStageKD;  // TMA-store staging (CL == 1), 1 KiB aligned
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -336,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if constexpr (CL == 1) tma_prefetch_desc(&tmC);
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(&tmem_slot), Cfg::kTmemCols);
@@ -465,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_in_tile = q * 32 + lane;
         const bool first_epi_thread = threadIdx.x == 64;
         int t_local = 0;
+        uint32_t boxes = 0;  // TMA-store boxes this warp has issued (selects its staging buffer)
         for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++t_local) {
             const int tile = unit / sk.splits;
             int mb, nb;
@@ -484,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int grow = mb * kBM + row_in_tile;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-            if (sk.splits == 1) {
+            if (sk.splits == 1 && Cfg::kEpiBytes == 0) {
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; ++c) {
                     uint32_t r[32];
@@ -492,6 +559,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_wait_ld();
                     const int gcol = nb * BN + c * 32;
                     if (grow < M && gcol < N) store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
+                continue;
+            }
+            if (sk.splits == 1) {
+                const int row0 = mb * kBM + q * 32;  // first row of this warp's boxes
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+                    tmem_wait_ld();
+                    const int gcol = nb * BN + c * 32;
+                    if (row0 >= M || gcol >= N) continue;  // warp-uniform: the box lies outside C
+                    const uint32_t buf = sEpi + (uint32_t)((q * 2 + (int)(boxes & 1u)) * epi_box_bytes<DT>());
+                    if (lane == 0) bulk_wait_read<1>();  // the store issued two boxes ago has read `buf`
+                    __syncwarp();
+                    stage_row<DT>(buf, lane, r, out_scale);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, buf, gcol, row0);
+                        bulk_commit();
+                    }
+                    ++boxes;
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -561,6 +654,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (first_epi_thread) sk.counters[tile] = 0u;  // ready for the next launch
         }
+        if (lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before the CTA exits
+        __syncwarp();
     }
 
     if constexpr (CL > 1) {
@@ -1075,7 +1170,12 @@ constexpr int kHalfN = kPairN / 2;                // B cols loaded per CTA
 constexpr int kPairStages = 6;
 constexpr int kPairAStage = kBM * kBKBytes;       // 16 KiB
 constexpr int kPairBStage = kHalfN * kBKBytes;    // 16 KiB
-constexpr size_t kPairSmemBytes = (size_t)kPairStages * (kPairAStage + kPairBStage) + 1024;
+constexpr size_t kPairRingBytes = (size_t)kPairStages * (kPairAStage + kPairBStage);
+// Ring, alignment slack and the epilogue's TMA-store staging.
+template <int DT>
+constexpr size_t pair_smem_bytes() {
+    return kPairRingBytes + 1024 + (size_t)epi_bytes<DT>();
+}
 
 __host__ __device__ constexpr uint32_t make_idesc_pair(uint32_t base_idesc) {
     // replace M (bits [24,29)) by 256
@@ -1093,7 +1193,8 @@ __device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uin
 template <int DT, bool KB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             void* __restrict__ C, int M, int N, int K, float out_scale, SplitK sk) {
+                             const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K,
+                             float out_scale, SplitK sk) {
     using Tr = Traits<DT>;
     constexpr int kBKElems = kBKBytes / Tr::kEsize;
     constexpr int kBoxN = 128 / Tr::kEsize;
@@ -1115,6 +1216,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = smem_base;
     const uint32_t sB = smem_base + kPairStages * kPairAStage;
+    const uint32_t sEpi = smem_base + (uint32_t)kPairRingBytes;  // TMA-store staging, 1 KiB aligned
 
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
@@ -1141,6 +1243,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmC);
     }
     if (warp == 0) {
         tmem_alloc_pair(smem_u32(&tmem_slot), kTmemCols);
@@ -1255,6 +1358,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t acce_leader0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
         const uint32_t acce_leader1 = mapa_shared(smem_u32(&acce_bar[1]), 0);
         int t_local = 0;
+        uint32_t boxes = 0;  // TMA-store boxes this warp has issued (selects its staging buffer)
         WorkItem it;
         for (int idx = 0; work_item(idx, pair, num_pairs, num_tiles, num_kb, sk, it); ++idx, ++t_local) {
             const int tile = it.tile;
@@ -1277,13 +1381,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kPairN);
             const uint32_t acce_remote = acc ? acce_leader1 : acce_leader0;
             if (it.slot < 0) {
+                const int row0 = mb * kPairM + (int)rank * kBM + q * 32;  // first row of this warp's boxes
 #pragma unroll 1
                 for (int c = 0; c < kPairN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
                     tmem_wait_ld();
                     const int gcol = nb * kPairN + c * 32;
-                    if (grow < M && gcol < N) store_chunk<DT>(C, grow, gcol, N, r, out_scale);
+                    if (row0 >= M || gcol >= N) continue;  // warp-uniform: the box lies outside C
+                    const uint32_t buf = sEpi + (uint32_t)((q * 2 + (int)(boxes & 1u)) * epi_box_bytes<DT>());
+                    if (lane == 0) bulk_wait_read<1>();  // the store issued two boxes ago has read `buf`
+                    __syncwarp();
+                    stage_row<DT>(buf, lane, r, out_scale);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, buf, gcol, row0);
+                        bulk_commit();
+                    }
+                    ++boxes;
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -1351,6 +1467,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (first_epi_thread) sk.counters[counter] = 0u;
         }
+        if (lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before teardown
+        __syncwarp();
     }
 
     // Teardown: the leader's MMAs read the peer's shared memory and write its
@@ -1577,10 +1695,11 @@ static int launch_ex(Kernel kernel, int grid, size_t smem, int cluster, cudaStre
 }
 
 template <int DT, bool KB, int BN, int CL = 1>
-static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, int n, int k, void* c,
-                         float out_scale, int splits, int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
+static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, int m, int n,
+                         int k, void* c, float out_scale, int splits, int dev, int sms, cudaStream_t stream,
+                         LaunchInfo* info) {
     using Tr = Traits<DT>;
-    using Cfg = TileCfg<BN, tile_kd(BN, CL, Tr::kEsize)>;
+    using Cfg = TileCfgFor<DT, BN, CL>;
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {
         TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, KB, BN, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1608,7 +1727,7 @@ static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, int m, 
         }
         grid = (int)std::max<long>(1, std::min<long>(tiles * splits, sms));
     }
-    const int rc = launch_ex(gemm_tcgen05_kernel<DT, KB, BN, CL>, grid, Cfg::kSmem, CL, stream, tmA, tmB, c, m, n, k,
+    const int rc = launch_ex(gemm_tcgen05_kernel<DT, KB, BN, CL>, grid, Cfg::kSmem, CL, stream, tmA, tmB, tmC, c, m, n, k,
                              out_scale, sk);
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaGetLastError());
@@ -1848,9 +1967,9 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         tile_n_single = bn;
     } else if (splits == 0 && cta_pair < 0 && tile_n_opt == 0) {
         auto capacity = [dev](int c) {
-            return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfg<256, 1>::kSmem, dev, 2)
-                   : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfg<256, 1>::kSmem, dev, 4)
-                            : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfg<256, 1>::kSmem, dev, 8);
+            return c == 2   ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 2>, TileCfgFor<DT, 256, 2>::kSmem, dev, 2)
+                   : c == 4 ? cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 4>, TileCfgFor<DT, 256, 4>::kSmem, dev, 4)
+                            : cluster_capacity(gemm_tcgen05_kernel<DT, KB, 256, 8>, TileCfgFor<DT, 256, 8>::kSmem, dev, 8);
         };
         const KernelChoice kc = choose_kernel(m, n, num_kb, KB || es >= 2, sms, capacity);
         pair_auto = kc.pair;
@@ -1872,26 +1991,31 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     else
         rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
+    // C as TMA-store boxes of 32 rows x 32 columns (whole-tile epilogues).
+    CUtensorMap tmC;
+    rc = encode_2d(&tmC, c, out_esize<DT>(), (uint64_t)n, (uint64_t)m, 32, 32,
+                   out_esize<DT>() == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TRB_OK) return rc;
     if (cluster > 1 && tile_n_single == 128) {
-        if (cluster == 2) return launch_single<DT, KB, 128, 2>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
-        return launch_single<DT, KB, 128, 4>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+        if (cluster == 2) return launch_single<DT, KB, 128, 2>(tmA, tmB, tmC, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+        return launch_single<DT, KB, 128, 4>(tmA, tmB, tmC, m, n, k, c, out_scale, 0, dev, sms, stream, info);
     }
-    if (cluster == 2) return launch_single<DT, KB, 256, 2>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
-    if (cluster == 4) return launch_single<DT, KB, 256, 4>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
-    if (cluster == 8) return launch_single<DT, KB, 256, 8>(tmA, tmB, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+    if (cluster == 2) return launch_single<DT, KB, 256, 2>(tmA, tmB, tmC, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+    if (cluster == 4) return launch_single<DT, KB, 256, 4>(tmA, tmB, tmC, m, n, k, c, out_scale, 0, dev, sms, stream, info);
+    if (cluster == 8) return launch_single<DT, KB, 256, 8>(tmA, tmB, tmC, m, n, k, c, out_scale, 0, dev, sms, stream, info);
     if (!pair) {
         if (tile_n == 64) {
             if constexpr (KB || es >= 2)
-                return launch_single<DT, KB, 64>(tmA, tmB, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+                return launch_single<DT, KB, 64>(tmA, tmB, tmC, m, n, k, c, out_scale, splits, dev, sms, stream, info);
         } else if (tile_n == 128) {
-            return launch_single<DT, KB, 128>(tmA, tmB, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+            return launch_single<DT, KB, 128>(tmA, tmB, tmC, m, n, k, c, out_scale, splits, dev, sms, stream, info);
         }
-        return launch_single<DT, KB, 256>(tmA, tmB, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+        return launch_single<DT, KB, 256>(tmA, tmB, tmC, m, n, k, c, out_scale, splits, dev, sms, stream, info);
     }
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {
         TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_pair_kernel<DT, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)kPairSmemBytes));
+                                      (int)pair_smem_bytes<DT>()));
         attr_set[dev] = true;
     }
     const int workers = sms / 2;
@@ -1911,8 +2035,8 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     const long units = tiles * splits;
     const int grid_workers = (int)std::max<long>(1, std::min<long>(units, workers));
     // The pair kernel's cluster shape (2 CTAs) is compiled in (__cluster_dims__).
-    rc = launch_ex(gemm_tcgen05_pair_kernel<DT, KB>, grid_workers * 2, kPairSmemBytes, 1, stream, tmA, tmB, c, m, n, k,
-                   out_scale, sk);
+    rc = launch_ex(gemm_tcgen05_pair_kernel<DT, KB>, grid_workers * 2, pair_smem_bytes<DT>(), 1, stream, tmA, tmB, tmC, c,
+                   m, n, k, out_scale, sk);
     if (rc != TRB_OK) return rc;
     TRB_CUDA(cudaGetLastError());
     if (info) {
@@ -2138,8 +2262,13 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     if (rc != TRB_OK) return rc;
     rc = encode_2d(&tmB, b, es, (uint64_t)n, (uint64_t)k, 128 / es, kBKBytes / es, Tr::BLayout::kTmaSwizzle);
     if (rc != TRB_OK) return rc;
+    CUtensorMap tmC;
+    rc = encode_2d(&tmC, c, out_esize<DT>(), (uint64_t)n, (uint64_t)m, 32, 32,
+                   out_esize<DT>() == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TRB_OK) return rc;
+    using Cfg = TileCfgFor<DT, 256, 1>;
     TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)TileCfg<256, 1>::kSmem));
+                                  (int)Cfg::kSmem));
     SplitK sk{splits, kbps, nullptr, nullptr, 0, 0};
     if (splits > 1) {
         // The array keeps the previous call's contents: counters must start at zero.
@@ -2149,8 +2278,8 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     }
     const long units = tiles * splits;
     const int grid = (int)std::max<long>(1, std::min<long>(units, sms));
-    gemm_tcgen05_kernel<DT, false, 256><<<grid, kThreads, TileCfg<256, 1>::kSmem, stream>>>(tmA, tmB, c, m, n, k,
-                                                                                         out_scale, sk);
+    gemm_tcgen05_kernel<DT, false, 256><<<grid, kThreads, Cfg::kSmem, stream>>>(tmA, tmB, tmC, c, m, n, k, out_scale,
+                                                                             sk);
     TRB_CUDA(cudaGetLastError());
     return TRB_OK;
 }
