@@ -715,6 +715,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
             }
         }
+        // Every partial sent to this CTA has landed (recv_bar) and its own sends
+        // are issued.  The exit barrier that keeps peers' shared memory alive
+        // while sends may still target it is split around the sum and stores,
+        // which hide its latency.
+        __syncwarp();
+        cluster_arrive();
         if (epi && ok) {
             int mb, nb;
             tile_coords((int)blockIdx.x / CL, num_m, num_n, sk.group_m, mb, nb);
@@ -752,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();
-        cluster_sync_all();  // no CTA leaves while a peer's stores may still target it
+        cluster_wait();  // no CTA leaves while a peer's stores may still target it
     }
 
     tc_fence_before();
