@@ -1662,14 +1662,19 @@ static KernelChoice choose_kernel(int m, int n, int num_kb, bool allow_bn64, int
 
 // Raster group: consecutive tiles walk down `group` m-blocks of one column
 // of tiles, so the group's A rows and one B column panel are what the
-// running tiles share in L2.  8 m-blocks measured best on B200 for the CTA
-// pair at 8192^3 and 16384^3 (bf16 1520 / 1514 TFLOP/s vs 1482 / 1465 with 16,
-// 1487 / 1419 with 4); the group's A rows are further kept under ~80 MB of
-// the 126 MB L2 for very long K.
+// running tiles share in L2.  Measured on B200 for the CTA pair:
+//  * A panels above 2 MB per m-block: 8 is best (bf16 8192^3 / 16384^3 1520 /
+//    1514 TFLOP/s vs 1482 / 1465 with 16 and 1487 / 1419 with 4; e4m3 16384^3
+//    3030 vs 2910 with 16);
+//  * panels of 2 MB or less take 16 (e4m3 8192^3 3049 vs 2997, bf16 4096^3
+//    1512 vs 1485, int8 8192^3 +1%);
+// single-CTA tiles (not measured with 16) keep 8; and the group's A rows are
+// kept under ~80 MB of the 126 MB L2 for very long K.
 static int raster_group(int rows_per_block, int k, int es) {
     const double a_bytes = (double)rows_per_block * k * es;
     const int g = (int)(80.0e6 / a_bytes);
-    return std::max(2, std::min(8, g));
+    const int cap = (rows_per_block == kPairM && a_bytes <= 2.1e6) ? 16 : 8;
+    return std::max(2, std::min(cap, g));
 }
 
 // Launch with programmatic stream serialization (the kernels' griddepcontrol
