@@ -5,16 +5,21 @@
 // mfu_gemm_highp.hip.hpp:39-218) and, for result semantics, the torch path's
 // torch.mm(a, b, out=out) (src/teamredbench/benchmarks/mfu.py:229-234).
 //
-// Design (one kernel template for all five input types):
-//  * persistent grid, one 192-thread CTA per SM, static tile schedule with
-//    grouped rasterisation (GROUP_M m-blocks share each B column panel in L2);
-//  * CTA tile 128 x 256, K staged 128 bytes at a time (64 bf16/f16, 32 tf32,
-//    128 e4m3/int8), 4-stage shared-memory ring fed by TMA (no multicast);
-//  * warp 0: TMA producer; warp 1: a single thread issues tcgen05.mma
-//    (cta_group::1, M=128, N=256, K=32 bytes per instruction) into a TMEM
-//    accumulator; warps 2-5: epilogue (tcgen05.ld -> convert -> global store);
-//  * two 256-column TMEM accumulators (512 columns) so the epilogue of tile i
-//    overlaps the main loop of tile i+1;
+// Design (kernel templates shared by all five input types):
+//  * persistent grid, one 192-thread CTA per SM (or CTA pair), static tile
+//    schedule with grouped rasterisation (group m-blocks share each B column
+//    panel in L2);
+//  * single-CTA tiles 128 x BN (BN = 256, 128, 64) and 256 x 256 CTA-pair
+//    tiles (cta_group::2); K moves in k-blocks of 128 bytes (64 bf16/f16, 32
+//    tf32, 128 e4m3/int8) through a ~192 KiB shared-memory ring fed by TMA (no
+//    multicast), several k-blocks per stage for the narrow tiles;
+//  * warp 0: TMA producer; warp 1: a single thread issues tcgen05.mma (32 K
+//    bytes per instruction) into a TMEM accumulator; warps 2-5: epilogue
+//    (tcgen05.ld -> convert -> shared staging -> TMA store for whole tiles);
+//  * two TMEM accumulators so the epilogue of tile i overlaps the main loop
+//    of tile i+1;
+//  * skinny problems (one row of tiles) use cluster split-K over distributed
+//    shared memory, or the swapped-operand kernel for M <= 64;
 //  * A is row-major (K-major operand, 128B swizzle); B is row-major K x N,
 //    i.e. an MN-major operand, consumed directly through the MN-major 128B
 //    swizzle layout (no re-layout pass: the reference needed an untimed
