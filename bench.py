@@ -152,25 +152,40 @@ def cpu_baseline_leg(torch_module) -> dict:
             "sample": f"float32 triad over 2^28 elements (3.2 GB per pass), {reps} passes, oracle/trb_oracle.c"}
 
 
+def host_threads() -> int:
+    """Every core this process may run on (torchrun's OMP_NUM_THREADS=1 does not apply here)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        return os.cpu_count() or 1
+
+
 def run_reference(args) -> None:
-    """The reference's torch-CPU triad on this host's cores (rank 0 only)."""
-    _, rank, _ = dist_setup(args.gpus)
+    """The reference's torch-CPU triad on this host's cores (rank 0 only; the
+    other ranks exit without work).  It runs with every host thread at every
+    N: the host's CPU path is one machine-wide resource, so N CPU replicas
+    would only split the same cores and DRAM bandwidth between them."""
+    world, rank, _ = dist_setup(args.gpus)
     if rank != 0:
         return
     import torch
 
     from oracle import reference_cpu
 
+    threads = host_threads()
+    torch.set_num_threads(threads)
     r = reference_cpu.time_hbm(torch, "triad", N_ELEMS, DTYPE, SCALE, args.warmup, args.steps)
     value = round(r["gbps"], 3)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": max(world, args.gpus),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["elapsed_s"] * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "hbm_triad_float32_2^30", "elements": N_ELEMS, "scale": SCALE,
-                   "path": "torch.add(b, c, alpha=s, out=a) on CPU (reference hbm.py:29-39)"},
+                   "path": "torch.add(b, c, alpha=s, out=a) on CPU (reference hbm.py:29-39)",
+                   "host_aggregate": "one process on every host thread; N CPU replicas would share these cores"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": r["threads"], "kind": "port",
-                         "sample": "full workload: float32 triad over 2^30 elements per step, torch CPU"},
+                         "sample": "full workload: float32 triad over 2^30 elements per step, torch CPU",
+                         "cpu_capability": torch.backends.cpu.get_cpu_capability()},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -277,6 +292,12 @@ def run_b200(args) -> None:
            "h2d_bytes_per_step": 2 * N_ELEMS * 4, "d2h_bytes_per_step": N_ELEMS * 4, "steps": e2e_steps,
            "path": "trb_hbm_host (pinned host buffers, 64 MiB chunks on 3 streams)"}
     del ha, hb, hc
+    torch.cuda.empty_cache()
+    e2e["roofline"] = e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e["value"],
+                                   e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"])
+
+    # ---- GEMM replicas (BASELINE metric: bf16 / fp8 MFU per GPU at 1/2/4/8 GPUs)
+    gemm_box = gemm_replicas(torch, dev, stream, barrier, max_over_ranks, world, local, dist)
 
     extras = {}
     if not args.no_extras:
@@ -299,9 +320,134 @@ def run_b200(args) -> None:
                    "variant": args.variant, "parallelism": f"replicas{world}",
                    "l2": "inputs 12 GiB per GPU >> 126 MB L2; no flush needed"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
-        "extras": extras,
+        "gemm_replicas": gemm_box, "extras": extras,
     }
     print(json.dumps(line), flush=True)
+
+
+def e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e_value, h2d_step, d2h_step) -> dict:
+    """What bounds `e2e`: pinned host<->device copies, measured on every rank at
+    once (1 GiB with cudaMemcpyAsync: H2D alone, D2H alone, and both directions
+    together on two streams).  A step moves h2d_step bytes in and d2h_step out,
+    which can overlap, so the fastest possible step takes the longer of the
+    two directions at their concurrent rates; the limit is the triad's
+    algorithmic bytes over that time, for all ranks together.  All ranks share
+    the host's DRAM, which also caps these copies."""
+    nbytes = 1 << 30
+    h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_in = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    d_out = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(h2d: bool, d2h: bool, reps: int = 3) -> float:
+        e0, e1, mid = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+                       torch.cuda.Event())
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0.record(s1)
+        s2.wait_event(e0)
+        for _ in range(reps):
+            if h2d:
+                with torch.cuda.stream(s1):
+                    d_in.copy_(h_in, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s2):
+                    h_out.copy_(d_out, non_blocking=True)
+        mid.record(s2)
+        s1.wait_event(mid)
+        e1.record(s1)
+        torch.cuda.synchronize(dev)
+        return max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps)
+
+    timed(True, True, 1)  # warm-up
+    t_h2d, t_d2h, t_both = timed(True, False), timed(False, True), timed(True, True)
+    h2d_gbps = world * nbytes / t_h2d / 1e9
+    d2h_gbps = world * nbytes / t_d2h / 1e9
+    both_each_gbps = world * nbytes / t_both / 1e9  # each direction, both running
+    step_s = max(h2d_step, d2h_step) * world / 1e9 / both_each_gbps
+    limit = world * BYTES_PER_STEP / step_s / 1e9
+    del h_in, h_out, d_in, d_out
+    torch.cuda.empty_cache()
+    return {"bound": "pcie (pinned host copies, all ranks at once)", "limit_gbps": round(limit, 2),
+            "frac": round(e2e_value / limit, 4), "h2d_gbps": round(h2d_gbps, 2), "d2h_gbps": round(d2h_gbps, 2),
+            "h2d_and_d2h_concurrent_gbps_each": round(both_each_gbps, 2),
+            "how": "1 GiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / "
+                   "(max(h2d, d2h) step bytes / concurrent per-direction rate)"}
+
+
+def gemm_replicas(torch, dev, stream, barrier, max_over_ranks, world, local, dist) -> dict:
+    """bf16 and fp8 (e4m3) 8192^3 GEMM on every GPU at once, one independent
+    replica per rank (BASELINE configs[2]/[3]; A, B ~ N(0,1)/sqrt(K), A drawn
+    first; fp8 with per-tensor scales absmax/448, bf16 output).  Two windows,
+    each bracketed by barrier + synchronize and timed with CUDA events, max over
+    ranks: a burst of 20 launches, and ~1.5 s of back-to-back launches under
+    the power cap with nvidia-smi clocks sampled on every rank."""
+    from teamredbench_b200.kernels import gemm
+
+    m = n = k = 8192
+    flops = 2.0 * m * n * k
+    nominal = {"bfloat16": 2250.0, "float8_e4m3fn": 4500.0}
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    for name in ("bfloat16", "float8_e4m3fn"):
+        a32 = torch.randn(m, k, generator=g, device=dev) / k ** 0.5
+        b32 = torch.randn(k, n, generator=g, device=dev) / k ** 0.5
+        if name == "bfloat16":
+            a, b, sa, sb = a32.to(torch.bfloat16), b32.to(torch.bfloat16), 1.0, 1.0
+        else:
+            sa, sb = float(a32.abs().max()) / 448.0, float(b32.abs().max()) / 448.0
+            a, b = (a32 / sa).to(torch.float8_e4m3fn), (b32 / sb).to(torch.float8_e4m3fn)
+        del a32, b32
+        c = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+
+        def run(iters):
+            for _ in range(iters):
+                gemm(a, b, c, dtype=name, scale_a=sa, scale_b=sb)
+
+        run(5)
+        torch.cuda.synchronize(dev)
+
+        def window(iters, sample=False):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            torch.cuda.synchronize(dev)
+            sampler = ClockSampler(local) if sample else None
+            if sampler:
+                sampler.__enter__()
+            e0.record(stream)
+            run(iters)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            if sampler:
+                sampler.__exit__(None, None, None)
+            barrier()
+            return max_over_ranks(e0.elapsed_time(e1) / 1e3), (sampler.summary() if sampler else None)
+
+        burst_iters = 20
+        t_burst, _ = window(burst_iters)
+        sus_iters = max(50, int(1.5 / (t_burst / burst_iters)))
+        sus_iters = int(max_over_ranks(float(sus_iters)))  # every rank runs the same count
+        t_sus, clocks = window(sus_iters, sample=True)
+        if dist is not None:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, clocks)
+        else:
+            gathered = [clocks]
+        box_burst = world * flops * burst_iters / t_burst / 1e12
+        box_sus = world * flops * sus_iters / t_sus / 1e12
+        out[name + "_8192"] = {
+            "burst_box_tflops": round(box_burst, 1), "burst_per_gpu_tflops": round(box_burst / world, 1),
+            "burst_mfu_pct_nominal": round(100 * box_burst / world / nominal[name], 2),
+            "sustained_box_tflops": round(box_sus, 1), "sustained_per_gpu_tflops": round(box_sus / world, 1),
+            "sustained_mfu_pct_nominal": round(100 * box_sus / world / nominal[name], 2),
+            "sustained_launches": sus_iters, "sustained_window_s": round(t_sus, 3),
+            "clocks_per_rank": [{kk: cl.get(kk) for kk in ("sm_mhz", "reasons", "power_w_max")} if cl else None
+                                for cl in gathered],
+        }
+        del a, b, c
+        torch.cuda.empty_cache()
+    return out
 
 
 def secondary_measurements(torch, dev, stream, peaks) -> dict:

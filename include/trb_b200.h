@@ -235,12 +235,18 @@ int trb_gemm_launch_ex(int dtype, int m, int n, int k, const void* a, const void
  * array in the library's device data, 16 KiB + 16 MiB, which every GPU that
  * loads the library holds until the process exits.
  *  - Limit: at most 128 tile-splits of 128 x 256 (e.g. M <= 128 with
- *    N * splits <= 32768) and 4096 output tiles; larger requests return
- *    TRB_ERR_ARGS with the sizes in trb_last_error().  splits = 0 picks the
- *    split count as trb_gemm_launch does (1 = no scratch used).
+ *    N * splits <= 32768) and 4096 output tiles; an explicit split count
+ *    beyond that returns TRB_ERR_ARGS with the sizes in trb_last_error().
+ *    splits = 0 takes the split count trb_gemm_launch_ex picks for the
+ *    single-CTA 128 x 256 kernel (splits = 0, cta_pair = 0), lowered to what
+ *    the array holds, so it never fails for lack of scratch (1 = no scratch
+ *    used).  It does not run trb_gemm_launch's automatic kernel choice
+ *    (CTA pair, cluster split-K, swapped operands).
  *  - The first call on a device resolves the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
+ *    (cudaGetSymbolAddress) with that device current and caches it; make that
+ *    first call before any stream capture.  Do not cudaDeviceReset a device
+ *    while the library is in use: the module reloads and the cached address
+ *    (like the library's other per-device state) goes stale.
  *  - All calls share the one array and it keeps the last call's contents
  *    (the counters are cleared by every call); calls that overlap on the GPU
  *    (other streams, other threads) race.
@@ -255,6 +261,20 @@ int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host, const void
 /* Round f32 values in place on the device to tf32 (round to nearest, ties
  * away from zero; cvt.rna.tf32.f32).  Used to prepare tf32 GEMM inputs. */
 int trb_round_tf32(void* data, uint64_t count, void* stream);
+
+/* Self-test of the device-side failure detector: launches one small kernel
+ * whose wait on an mbarrier that nothing arrives on gives up after limit_us
+ * microseconds (1 .. 1e6) -- the same bounded wait, error word and CTA abort
+ * flag every GEMM kernel uses, with a short limit instead of 2 s -- while a
+ * second waiter, on the full limit, leaves as soon as it sees the abort flag.
+ * Returns TRB_ERR_DEVICE_TIMEOUT with out->device_error = 6 (and
+ * out->elapsed_s near limit_us) when the detector works; TRB_OK would mean
+ * the wait did not give up.  No fault, trap or hang is involved, and the
+ * context stays usable: the next launch runs normally.  Clears the error
+ * words before and after.  No counterpart in the reference, whose native
+ * kernels have no bounded waits and whose runner has no timeout
+ * (src/teamredbench/native/runtime.py:281-287). */
+int trb_selftest_bounded_wait(uint32_t limit_us, int device_id, trb_result* out);
 
 #ifdef __cplusplus
 }

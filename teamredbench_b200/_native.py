@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "trb_gemm_launch_noalloc",
     "trb_gemm_host",
     "trb_round_tf32",
+    "trb_selftest_bounded_wait",
 )
 
 
@@ -169,6 +170,8 @@ def load() -> ctypes.CDLL:
     lib.trb_gemm_host.restype = i32
     lib.trb_round_tf32.argtypes = [vp, u64, vp]
     lib.trb_round_tf32.restype = i32
+    lib.trb_selftest_bounded_wait.argtypes = [ctypes.c_uint32, i32, res_p]
+    lib.trb_selftest_bounded_wait.restype = i32
     _lib = lib
     return lib
 
@@ -248,6 +251,15 @@ def gemm_host(dtype: str, m: int, n: int, k: int, a: int, b: int, c: int, scale_
 
 def round_tf32(data: int, count: int, stream: int = 0) -> None:
     check(load().trb_round_tf32(data, count, stream or None))
+
+
+def selftest_bounded_wait(limit_us: int, device_id: int = 0) -> tuple[int, TrbResult, str]:
+    """Run the bounded-wait self-test kernel (trb_selftest_bounded_wait);
+    returns (status, result, last error message) without raising, since the
+    expected status is TRB_ERR_DEVICE_TIMEOUT."""
+    result = TrbResult()
+    status = load().trb_selftest_bounded_wait(limit_us, device_id, ctypes.byref(result))
+    return status, result, last_error()
 
 
 def device_error(device_id: int = 0, clear: bool = False) -> int:

@@ -9,18 +9,21 @@ replaces it.  Additions over the reference:
   * `bus_factor_nccl_tests` (all_gather's (n-1)/n applied to the gathered
     total, as nccl-tests does) beside the reference's per-rank convention;
   * `preallocate_outputs: true` to keep all_gather's output allocation out of
-    the timed loop (the reference allocates inside it).
+    the timed loop (the reference allocates inside it);
+  * `elapsed_s` is device time (CUDA events around the timed loop), the max
+    over ranks; the reference's host timing of the same loop is kept as
+    `host_elapsed_s`.
 Bus factors (reference :12-16): all_reduce 2(n-1)/n, all_gather (n-1)/n,
 broadcast 1."""
 from __future__ import annotations
 
 import socket
+import time
 from typing import Any
 
 from teamredbench_b200.benchmarks.base import Benchmark, BenchmarkRecord
 from teamredbench_b200.device import cuda_device_available
 from teamredbench_b200.registry import register_benchmark
-from teamredbench_b200.utils import timed_iterations
 
 BUS_FACTORS = {
     "all_reduce": lambda world_size: 2 * (world_size - 1) / world_size,
@@ -90,6 +93,29 @@ class CollectiveBandwidthBenchmark(Benchmark):
                                  dtype=dtype)
         return (torch.rand(numel, device=self.device, generator=g) * 2 - 1).to(dtype)
 
+    def _time_loop(self, dist: Any, fn, warmup: int, iterations: int) -> tuple[float, float]:
+        """Mean seconds per collective, max over ranks: device time from CUDA
+        events on the current stream (which NCCL's blocking collectives make
+        wait for their own stream), and the reference's host timing of the same
+        loop (timed_iterations' rule: perf_counter between two synchronizes,
+        src/teamredbench/utils.py:14-29)."""
+        torch = self.torch
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        start.record()
+        for _ in range(iterations):
+            fn()
+        stop.record()
+        torch.cuda.synchronize()
+        host = (time.perf_counter() - t0) / max(iterations, 1)
+        device = start.elapsed_time(stop) / 1e3 / max(iterations, 1)
+        both = torch.tensor([device, host], dtype=torch.float64, device=self.device)
+        dist.all_reduce(both, op=dist.ReduceOp.MAX)
+        return float(both[0].item()), float(both[1].item())
+
     def run(self) -> list[BenchmarkRecord]:
         if self.context.torch_module is None:
             return [self.emit_record(self.skipped_record(case="global", dtype="n/a", error="PyTorch is not installed."))]
@@ -127,9 +153,10 @@ class CollectiveBandwidthBenchmark(Benchmark):
                         gather = ([torch.empty_like(tensor) for _ in range(world_size)]
                                   if preallocate and op_name == "all_gather" else None)
                         dist.barrier()
-                        elapsed_s = timed_iterations(lambda: self._run_collective(op_name, dist, tensor, gather),
-                                                     torch_module=torch, warmup=warmup, iterations=iterations)
+                        elapsed_s, host_s = self._time_loop(
+                            dist, lambda: self._run_collective(op_name, dist, tensor, gather), warmup, iterations)
                         dist.barrier()
+                        del tensor, gather
                     except Exception as exc:  # noqa: BLE001
                         records.append(self.emit_record(self.skipped_record(
                             case=case, dtype=spec.name, error=str(exc),
@@ -139,6 +166,7 @@ class CollectiveBandwidthBenchmark(Benchmark):
                         benchmark=self.name, case=case, dtype=spec.name,
                         raw_metrics={
                             "elapsed_s": elapsed_s,
+                            "host_elapsed_s": host_s,
                             "payload_bytes": numel * spec.bytes_per_element,
                             "bus_factor": BUS_FACTORS[op_name](world_size),
                             "bus_factor_nccl_tests": NCCL_TESTS_BUS_FACTORS[op_name](world_size),

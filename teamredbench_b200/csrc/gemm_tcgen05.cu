@@ -300,7 +300,73 @@ struct SplitK {
     unsigned int* counters;
     int rotate_k;  // 1: start each tile's K loop at k-block (tile % nk) and wrap
     int group_m;   // m-blocks per raster group (consecutive tiles walk down a group's column)
+    int chunk_kb;  // > 0: K-chunked accumulation, chunk_kb k-blocks per chain (below); 0: one chain per unit
 };
+
+// ---- K-chunked accumulation (tf32 inputs: tf32 and the float32 path) ----
+// The tensor core's fp32 accumulation error grows with the length of one
+// accumulation chain.  Measured on B200 with tf32-exact N(0,1)/sqrt(K) inputs
+// (max |C - C_fp64| / max |C_fp64|, K-chunks of one chain): 5.2e-6 for 2048 K
+// elements, 8.0e-6 for ~2730, 1.1e-5 for 4096, 2.2e-5 for 8192 -- and cuBLAS's
+// tf32 GEMM gives the same 2.2e-5 at K = 8192.  With chunk_kb > 0 a unit's K
+// range runs as chunks of chunk_kb k-blocks: the MMA thread accumulates each
+// chunk from zero into the TMEM accumulator the previous chunk did not use,
+// and the epilogue folds every completed chunk into the running sum held in
+// the other accumulator, cur += prev in fp32 on the CUDA cores (round to
+// nearest), then frees prev for the chunk after next.  The last chunk's
+// accumulator then holds the unit's sum and takes the usual epilogue path.
+// Chunks count k-block positions from the unit's start, so the chains -- and
+// the bits of the result -- do not depend on the launch shape.
+__host__ __device__ __forceinline__ int unit_chunks(int nk, int chunk_kb) {
+    return chunk_kb > 0 && nk > chunk_kb ? (nk + chunk_kb - 1) / chunk_kb : 1;
+}
+// k-blocks per accumulation chain: 64 k-blocks = 2048 tf32 elements for tf32
+// inputs (a multiple of every ring's k-blocks per stage); one chain per unit
+// for the other kinds (fp32 accumulation of 16/8-bit inputs is far inside
+// their 1e-2 bound; int8 accumulates exactly in s32).
+template <int DT>
+constexpr int chain_kb() {
+    return DT == TRB_TFLOAT32 ? 64 : 0;
+}
+
+// cur += prev over COLS accumulator columns of this warp's 32 TMEM lanes
+// (t_prev / t_cur: lane-quarter base addresses of the two accumulators), 64
+// columns per TMEM round trip.  `release` runs as soon as the last columns of
+// prev are in registers -- before the last sums are stored -- so the MMA
+// thread, which waits for prev to start the chunk after next, restarts early.
+template <int COLS, typename Release>
+__device__ __forceinline__ void fold_chunk(uint32_t t_prev, uint32_t t_cur, Release release) {
+    if constexpr (COLS == 16 || COLS == 32) {
+        uint32_t p[COLS], r[COLS];
+        if constexpr (COLS == 16) {
+            tmem_ld_32x32b_x16(t_prev, p);
+            tmem_ld_32x32b_x16(t_cur, r);
+        } else {
+            tmem_ld_32x32b_x32(t_prev, p);
+            tmem_ld_32x32b_x32(t_cur, r);
+        }
+        tmem_wait_ld();
+        release();
+#pragma unroll
+        for (int i = 0; i < COLS; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(p[i]));
+        if constexpr (COLS == 16) tmem_st_32x32b_x16(t_cur, r);
+        else tmem_st_32x32b_x32(t_cur, r);
+    } else {
+        static_assert(COLS % 64 == 0, "fold width");
+#pragma unroll 1
+        for (int c = 0; c < COLS / 64; ++c) {
+            uint32_t p[64], r[64];
+            tmem_ld_32x32b_x64(t_prev + (uint32_t)(c * 64), p);
+            tmem_ld_32x32b_x64(t_cur + (uint32_t)(c * 64), r);
+            tmem_wait_ld();
+            if (c == COLS / 64 - 1) release();
+#pragma unroll
+            for (int i = 0; i < 64; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(p[i]));
+            tmem_st_32x32b_x64(t_cur + (uint32_t)(c * 64), r);
+        }
+    }
+    tmem_wait_st();
+}
 
 // One unit of a worker's schedule: a k-block range of a tile.  slot >= 0: the
 // tile is split and this range's fp32 partial goes to workspace slot `slot`
@@ -487,17 +553,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++t_local) {
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
                 const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
-                const int acc = t_local & 1;
-                const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
-                if (!mbar_wait(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
-                    atomicCAS(&g_gemm_error, 0, kErrMmaWait);
-                    abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                const int chunk = unit_chunks(nk, sk.chunk_kb) > 1 ? sk.chunk_kb : nk;  // a multiple of kKD
+                int acc = 0, chunk_left = 0;
+                uint32_t d_tmem = tmem_base;
                 for (int i0 = 0; i0 < nk; i0 += kKD) {  // same stages as the producer; only the counts matter here
                     const int cnt = min(kKD, nk - i0);
+                    if (chunk_left == 0) {  // a chunk starts: take the next accumulator, zero it by its first MMA
+                        if (i0 != 0) {
+                            tc_commit(smem_u32(&accf_bar[acc]));  // chunk complete -> epilogue folds it
+                            ++t_local;
+                        }
+                        acc = t_local & 1;
+                        if (!mbar_wait(smem_u32(&acce_bar[acc]), ((uint32_t)(t_local >> 1) & 1u) ^ 1u, &abort_flag)) {
+                            atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                            abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        d_tmem = tmem_base + (uint32_t)(acc * BN);
+                        chunk_left = chunk;
+                    }
+                    const bool fresh = chunk_left == chunk;
+                    chunk_left -= cnt;
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
@@ -515,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int ks = 0; ks < kKSteps; ++ks)
                             mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)((d * kAStage + ks * kInstrKBytes) >> 4),
                                            b_stage + (uint64_t)((d * kBStageT + ks * kBKStep) >> 4), kIdesc1,
-                                           (i0 != 0 || d != 0 || ks != 0) ? 1u : 0u);
+                                           (!fresh || d != 0 || ks != 0) ? 1u : 0u);
                     }
                     tc_commit(smem_u32(&empty_bar[stage]));  // frees the smem stage when these MMAs finish
                     if (++stage == kStagesT) {
@@ -537,15 +615,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool first_epi_thread = threadIdx.x == 64;
         int t_local = 0;
         uint32_t boxes = 0;  // TMA-store boxes this warp has issued (selects its staging buffer)
+        const uint32_t t_quarter = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++t_local) {
             const int tile = unit / sk.splits;
             int mb, nb;
             tile_coords(tile, num_m, num_n, sk.group_m, mb, nb);
-            const int acc = t_local & 1;
-            const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
-            bool ok = mbar_wait(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
-            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);  // the fix-up below is CTA-wide
+            const int kb0 = (unit % sk.splits) * sk.kb_per_split;
+            const int nch = unit_chunks(min(kb0 + sk.kb_per_split, num_kb) - kb0, sk.chunk_kb);
+            bool ok = true;
+            for (int ch = 0; ch < nch; ++ch) {  // K chunks: fold each into the running sum
+                if (ch > 0) ++t_local;
+                const int a = t_local & 1;
+                ok = mbar_wait(smem_u32(&accf_bar[a]), (uint32_t)(t_local >> 1) & 1u, &abort_flag);
+                ok = __all_sync(0xffffffffu, ok);
+                if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);  // the fix-up below is CTA-wide
+                if (!ok) break;
+                tc_fence_after();
+                if (ch > 0) {
+                    fold_chunk<BN>(t_quarter + (uint32_t)((a ^ 1) * BN), t_quarter + (uint32_t)(a * BN), [&] {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(&acce_bar[a ^ 1]));  // running sum read: free it
+                    });
+                }
+            }
             if (!ok) {
                 if (lane == 0) {
                     atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
@@ -553,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 break;
             }
-            tc_fence_after();
+            const int acc = t_local & 1;
             const int grow = mb * kBM + row_in_tile;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
             if (sk.splits == 1 && Cfg::kEpiBytes == 0) {
@@ -669,14 +762,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int row_in_tile = q * 32 + lane;
         bool ok = true;
+        int acc = 0;  // accumulator holding this CTA's partial after the chunk folds
         if (epi) {
             grid_dependency_wait();
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf_bar[0]), 0, &abort_flag));
+            const int kb0 = (int)(blockIdx.x % CL) * sk.kb_per_split;
+            const int nch = unit_chunks(min(kb0 + sk.kb_per_split, num_kb) - kb0, sk.chunk_kb);
+            const uint32_t t_quarter = tmem_base + ((uint32_t)(q * 32) << 16);
+            for (int ch = 0; ch < nch; ++ch) {  // one unit per CTA: chunk ch uses accumulator ch & 1
+                acc = ch & 1;
+                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf_bar[acc]), (uint32_t)(ch >> 1) & 1u, &abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+                if (ch > 0) {
+                    fold_chunk<BN>(t_quarter + (uint32_t)((acc ^ 1) * BN), t_quarter + (uint32_t)(acc * BN), [&] {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc ^ 1]));
+                    });
+                }
+            }
             if (!ok && lane == 0) {
                 atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
                 abort_flag = 1;
             }
-            tc_fence_after();
         }
         __syncwarp();
         cluster_sync_all();  // every CTA's MMAs and TMA writes are done: the rings can receive
@@ -693,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (epi && ok) {
             if (threadIdx.x == 64) mbar_arrive_expect_tx(recv_bar_addr, (uint32_t)((CL - 1) * kOwnCols * kBM * 4));
             uint4* recv4 = reinterpret_cast<uint4*>(smem_raw + (sRecv - smem_u32(smem_raw)));
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16);
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
@@ -978,17 +1086,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x, ++t_local) {
                 const int kb0 = (unit % sk.splits) * sk.kb_per_split;
                 const int nk = min(kb0 + sk.kb_per_split, num_kb) - kb0;
-                const int acc = t_local & 1;
-                const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
-                if (!mbar_wait(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
-                    atomicCAS(&g_gemm_error, 0, kErrMmaWait);
-                    abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BS);
+                const int chunk = unit_chunks(nk, sk.chunk_kb) > 1 ? sk.chunk_kb : nk;  // a multiple of KD
+                int acc = 0, chunk_left = 0;
+                uint32_t d_tmem = tmem_base;
                 for (int g = 0; g * KD < nk; ++g) {
                     const int valid = min(KD, nk - g * KD);
+                    if (chunk_left == 0) {  // a chunk starts: take the next accumulator, zero it by its first MMA
+                        if (g != 0) {
+                            tc_commit(smem_u32(&accf_bar[acc]));
+                            ++t_local;
+                        }
+                        acc = t_local & 1;
+                        if (!mbar_wait(smem_u32(&acce_bar[acc]), ((uint32_t)(t_local >> 1) & 1u) ^ 1u, &abort_flag)) {
+                            atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                            abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        d_tmem = tmem_base + (uint32_t)(acc * BS);
+                        chunk_left = chunk;
+                    }
+                    const bool fresh = chunk_left == chunk;
+                    chunk_left -= valid;
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
@@ -1002,7 +1122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int ks = 0; ks < kKSteps; ++ks)
                             mma<Tr::kKind>(d_tmem, a_stage + (uint64_t)((i * kWBlock + ks * kWStep) >> 4),
                                            b_stage + (uint64_t)((i * kSBlock + ks * kInstrKBytes) >> 4), kIdescS,
-                                           (g != 0 || i != 0 || ks != 0) ? 1u : 0u);
+                                           (!fresh || i != 0 || ks != 0) ? 1u : 0u);
                     }
                     tc_commit(smem_u32(&empty_bar[stage]));
                     if (++stage == kStagesT) {
@@ -1023,13 +1143,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool first_epi_thread = threadIdx.x == 64;
         const int rows = M < BS ? M : BS;
         int t_local = 0;
+        const uint32_t t_quarter = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++t_local) {
             const int tile = unit / sk.splits;
-            const int acc = t_local & 1;
-            const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
-            bool ok = mbar_wait(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
-            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);
+            const int kb0 = (unit % sk.splits) * sk.kb_per_split;
+            const int nch = unit_chunks(min(kb0 + sk.kb_per_split, num_kb) - kb0, sk.chunk_kb);
+            bool ok = true;
+            for (int ch = 0; ch < nch; ++ch) {  // K chunks: fold each into the running sum
+                if (ch > 0) ++t_local;
+                const int a = t_local & 1;
+                ok = mbar_wait(smem_u32(&accf_bar[a]), (uint32_t)(t_local >> 1) & 1u, &abort_flag);
+                ok = __all_sync(0xffffffffu, ok);
+                if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);
+                if (!ok) break;
+                tc_fence_after();
+                if (ch > 0) {
+                    fold_chunk<BS>(t_quarter + (uint32_t)((a ^ 1) * BS), t_quarter + (uint32_t)(a * BS), [&] {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(&acce_bar[a ^ 1]));  // running sum read: free it
+                    });
+                }
+            }
             if (!ok) {
                 if (lane == 0) {
                     atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
@@ -1037,7 +1172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 break;
             }
-            tc_fence_after();
+            const int acc = t_local & 1;
             const int gn = tile * kBM + n_in_tile;
             uint32_t r[BS];
             tmem_ld_row<BS>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BS), r);
@@ -1326,16 +1461,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             WorkItem it;
             for (int idx = 0; ok && work_item(idx, pair, num_pairs, num_tiles, num_kb, sk, it); ++idx, ++t_local) {
                 const int kb0 = it.kb0, kb1 = it.kb1;
-                const int acc = t_local & 1;
-                const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
-                if (!mbar_wait_cluster(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, &abort_flag)) {
-                    atomicCAS(&g_gemm_error, 0, kErrMmaWait);
-                    abort_flag = 1;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kPairN);
+                const int chunk = unit_chunks(kb1 - kb0, sk.chunk_kb) > 1 ? sk.chunk_kb : kb1 - kb0;
+                int acc = 0, chunk_left = 0;
+                uint32_t d_tmem = tmem_base;
                 for (int kb = kb0; kb < kb1; ++kb) {
+                    if (chunk_left == 0) {  // a chunk starts: take the next accumulator, zero it by its first MMA
+                        if (kb != kb0) {
+                            tc_commit_pair_multicast(smem_u32(&accf_bar[acc]), 0x3);  // both CTAs fold it
+                            ++t_local;
+                        }
+                        acc = t_local & 1;
+                        if (!mbar_wait_cluster(smem_u32(&acce_bar[acc]), ((uint32_t)(t_local >> 1) & 1u) ^ 1u,
+                                               &abort_flag)) {
+                            atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                            abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        d_tmem = tmem_base + (uint32_t)(acc * kPairN);
+                        chunk_left = chunk;
+                    }
+                    const bool fresh = chunk_left == chunk;
+                    --chunk_left;
                     if (!mbar_wait_cluster(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
                         abort_flag = 1;
@@ -1348,7 +1496,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (int ks = 0; ks < kKSteps; ++ks)
                         mma_pair<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kInstrKBytes >> 4),
                                             b_stage + (uint64_t)(ks * kBKStep >> 4), kIdesc,
-                                            (kb != kb0 || ks != 0) ? 1u : 0u);
+                                            (!fresh || ks != 0) ? 1u : 0u);
                     tc_commit_pair_multicast(smem_u32(&empty_bar[stage]), 0x3);
                     if (++stage == kPairStages) {
                         stage = 0;
@@ -1371,15 +1519,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int t_local = 0;
         uint32_t boxes = 0;  // TMA-store boxes this warp has issued (selects its staging buffer)
         WorkItem it;
+        const uint32_t t_quarter = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int idx = 0; work_item(idx, pair, num_pairs, num_tiles, num_kb, sk, it); ++idx, ++t_local) {
             const int tile = it.tile;
             int mb, nb;
             tile_coords(tile, num_m, num_n, sk.group_m, mb, nb);
-            const int acc = t_local & 1;
-            const uint32_t acc_phase = (uint32_t)(t_local >> 1) & 1u;
-            bool ok = mbar_wait_cluster(smem_u32(&accf_bar[acc]), acc_phase, &abort_flag);
-            ok = __all_sync(0xffffffffu, ok);
-            if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);  // the fix-up below is CTA-wide
+            const int nch = unit_chunks(it.kb1 - it.kb0, sk.chunk_kb);
+            bool ok = true;
+            for (int ch = 0; ch < nch; ++ch) {  // K chunks: fold each into the running sum (this CTA's half)
+                if (ch > 0) ++t_local;
+                const int a = t_local & 1;
+                ok = mbar_wait_cluster(smem_u32(&accf_bar[a]), (uint32_t)(t_local >> 1) & 1u, &abort_flag);
+                ok = __all_sync(0xffffffffu, ok);
+                if (sk.splits > 1) ok = named_barrier_and(1, 128, ok);  // the fix-up below is CTA-wide
+                if (!ok) break;
+                tc_fence_after();
+                if (ch > 0) {
+                    fold_chunk<kPairN>(t_quarter + (uint32_t)((a ^ 1) * kPairN), t_quarter + (uint32_t)(a * kPairN),
+                                       [&] {
+                                           tc_fence_before();
+                                           __syncwarp();
+                                           if (lane == 0) mbar_arrive_cluster(a ? acce_leader0 : acce_leader1);
+                                       });
+                }
+            }
             if (!ok) {
                 if (lane == 0) {
                     atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
@@ -1387,7 +1550,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 break;
             }
-            tc_fence_after();
+            const int acc = t_local & 1;
             const int grow = mb * kPairM + (int)rank * kBM + row_in_tile;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kPairN);
             const uint32_t acce_remote = acc ? acce_leader1 : acce_leader0;
@@ -1724,7 +1887,7 @@ static int launch_single(const CUtensorMap& tmA, const CUtensorMap& tmB, const C
     }
     const long tiles = (long)((m + kBM - 1) / kBM) * ((n + BN - 1) / BN);
     const int num_kb = (int)(((long)k * Tr::kEsize + kBKBytes - 1) / kBKBytes);
-    SplitK sk{1, num_kb, nullptr, nullptr, m <= kBM ? 1 : 0, raster_group(kBM, k, Tr::kEsize)};
+    SplitK sk{1, num_kb, nullptr, nullptr, m <= kBM ? 1 : 0, raster_group(kBM, k, Tr::kEsize), chain_kb<DT>()};
     int grid;
     if constexpr (CL > 1) {
         sk.splits = CL;
@@ -1831,7 +1994,7 @@ static int launch_swap(const void* a, const void* b, int m, int n, int k, void* 
     // No K rotation: the S box is only BS x 128 bytes, and CTAs that walk K in
     // step read whole rows of B together (measured 29.1 vs 30.7 us at
     // M = 16, N = K = 8192 bf16 with per-tile rotation).
-    SplitK sk{1, num_kb, nullptr, nullptr, 0, 0};
+    SplitK sk{1, num_kb, nullptr, nullptr, 0, 0, chain_kb<DT>()};
     int grid;
     if constexpr (CL > 1) {
         sk.splits = CL;
@@ -2040,7 +2203,7 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     splits = std::max(1, std::min(splits, num_kb));
     const int kbps = (num_kb + splits - 1) / splits;
     splits = (num_kb + kbps - 1) / kbps;
-    SplitK sk{splits, kbps, nullptr, nullptr, 0, raster_group(kPairM, k, es)};
+    SplitK sk{splits, kbps, nullptr, nullptr, 0, raster_group(kPairM, k, es), chain_kb<DT>()};
     // (A stream-K tail -- the last partial wave's tiles spread over all pairs in
     // equal k-block ranges -- measured 15-45% slower than whole tiles at 4096^3
     // and 3072 x 4096 x 2048 on B200, and was dropped.)
@@ -2225,7 +2388,11 @@ static std::mutex g_noalloc_mu;
 
 // Host code cannot use g_noalloc_scratch's name as a device address (it names
 // a host-side shadow); the device address comes from cudaGetSymbolAddress,
-// resolved once per device while that device is current.
+// resolved once per device while that device is current and cached for the
+// life of the process.  A cudaDeviceReset (or any teardown of the primary
+// context) while the library is in use reloads the module and can move the
+// array, so the cached address would be stale; the header forbids it, as it
+// would also invalidate the library's other per-device state.
 static int noalloc_scratch(int dev, NoAllocScratch* out) {
     if (dev < 0 || dev >= 64) {
         set_error("trb_gemm_launch_noalloc: device id %d out of range", dev);
@@ -2258,7 +2425,14 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     const int sms = device_sm_count(dev);
     const long tiles = (long)((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
     const int num_kb = (int)(((long)k * es + kBKBytes - 1) / kBKBytes);
-    if (splits <= 0) splits = choose_splits(tiles, num_kb, sms);
+    if (splits <= 0) {
+        // Automatic: choose_splits' count, cut to what the fixed scratch holds
+        // (an automatic request never fails for lack of scratch).
+        constexpr long kUnits = (long)(kNoAllocPartialBytes / (kBM * kBN * sizeof(float)));
+        splits = choose_splits(tiles, num_kb, sms);
+        if (tiles > (long)(kNoAllocCounterBytes / sizeof(unsigned int))) splits = 1;
+        splits = (int)std::min<long>(splits, std::max<long>(1, kUnits / std::max<long>(tiles, 1)));
+    }
     splits = std::max(1, std::min(splits, num_kb));
     const int kbps = (num_kb + splits - 1) / splits;
     splits = (num_kb + kbps - 1) / kbps;
@@ -2285,7 +2459,9 @@ static int launch_noalloc_typed(int m, int n, int k, const void* a, const void* 
     using Cfg = TileCfgFor<DT, 256, 1>;
     TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<DT, false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)Cfg::kSmem));
-    SplitK sk{splits, kbps, nullptr, nullptr, 0, 0};
+    // K rotation and raster as trb_gemm_launch_ex's single-CTA 128 x 256
+    // kernel (launch_single), so the two agree bit for bit at equal splits.
+    SplitK sk{splits, kbps, nullptr, nullptr, m <= kBM ? 1 : 0, raster_group(kBM, k, es), chain_kb<DT>()};
     if (splits > 1) {
         // The array keeps the previous call's contents: counters must start at zero.
         TRB_CUDA(cudaMemsetAsync(scratch.counters, 0, counter_bytes, stream));
@@ -2417,6 +2593,55 @@ int fill_operand(void* data, int dtype, uint64_t n, int k, uint64_t seed, unsign
         return TRB_OK;
     }
     fill_gemm_kernel<<<grid, 256, 0, stream>>>(data, dtype, n, seed, inv_sqrt_k, nullptr);
+    TRB_CUDA(cudaGetLastError());
+    return TRB_OK;
+}
+
+// Bounded-wait self-test: the failure path of every GEMM kernel's waits, made
+// to run on purpose without a fault.  Warp 0 holds TMEM (as the GEMM kernels
+// do) and its lane 0 waits, with the library's bounded wait and a short limit,
+// for the first phase of an mbarrier that nothing ever arrives on; it gives
+// up, records kErrSelfTestWait in the module's error word and raises the
+// CTA's abort flag.  Warp 1's lane 0 waits on a second such barrier with the
+// full kWaitTimeoutNs limit and returns as soon as it sees the abort flag --
+// the path by which one stalled role releases the others.  No TMA, MMA or
+// other asynchronous operation is in flight; TMEM is freed before exit.
+__global__ void __launch_bounds__(64, 1) wait_probe_kernel(uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t never_bar[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&never_bar[0]), 1);
+        mbar_init(smem_u32(&never_bar[1]), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&tmem_slot), 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+        if (!mbar_wait(smem_u32(&never_bar[0]), 0, &abort_flag, limit_ns)) {
+            atomicCAS(&g_gemm_error, 0, kErrSelfTestWait);
+            abort_flag = 1;
+        }
+    } else if (threadIdx.x == 32) {
+        if (!mbar_wait(smem_u32(&never_bar[1]), 0, &abort_flag)) atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_slot, 32);
+    }
+}
+
+int wait_probe(uint64_t limit_ns, cudaStream_t stream) {
+    wait_probe_kernel<<<1, 64, 0, stream>>>(limit_ns);
     TRB_CUDA(cudaGetLastError());
     return TRB_OK;
 }

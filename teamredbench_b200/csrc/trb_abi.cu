@@ -538,3 +538,39 @@ extern "C" int trb_gemm_host(int dtype, int m, int n, int k, const void* a_host,
     gemm_impl_name(info, out->implementation, sizeof(out->implementation), "+copies");
     return check_device_errors(out);
 }
+
+extern "C" int trb_selftest_bounded_wait(uint32_t limit_us, int device_id, trb_result* out) {
+    clear_error();
+    if (out == nullptr || limit_us == 0 || limit_us > 1000000u) {
+        set_error("trb_selftest_bounded_wait: limit_us must be in 1..1000000");
+        return TRB_ERR_ARGS;
+    }
+    int rc = set_device(device_id);
+    if (rc != TRB_OK) return rc;
+    fill_result_common(out, device_id);
+    // Words left by earlier calls would be reported as this probe's.
+    if (hbm::read_error(true) < 0 || gemm::read_error(true) < 0) return TRB_ERR_CUDA;
+    cudaStream_t s = nullptr;
+    cudaEvent_t start = nullptr, stop = nullptr;
+    TRB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    TRB_CUDA(cudaEventCreate(&start));
+    TRB_CUDA(cudaEventCreate(&stop));
+    TRB_CUDA(cudaEventRecord(start, s));
+    rc = gemm::wait_probe((uint64_t)limit_us * 1000ull, s);
+    if (rc == TRB_OK) {
+        TRB_CUDA(cudaEventRecord(stop, s));
+        TRB_CUDA(cudaEventSynchronize(stop));
+        float ms = 0.f;
+        TRB_CUDA(cudaEventElapsedTime(&ms, start, stop));
+        out->elapsed_s = ms / 1000.0;
+        out->grid = 1;
+        out->block = 64;
+        out->launches = 1;
+        snprintf(out->implementation, sizeof(out->implementation), "bounded_wait_probe");
+    }
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    cudaStreamDestroy(s);
+    if (rc != TRB_OK) return rc;
+    return check_device_errors(out);
+}

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests.helpers import GEMM_OUT, gemm_operands, gemm_result_f64, gemm_tolerance, to_raw, torch_dtype
+from tests.helpers import GEMM_OUT, GEMM_TOLERANCE, gemm_operands, gemm_result_f64, to_raw, torch_dtype
 
 pytestmark = pytest.mark.gpu
 
@@ -62,6 +62,6 @@ def test_random_gemm_matches_oracle(seed):
     if name == "int8":
         assert np.array_equal(got.astype(np.int64), ref.astype(np.int64)), (m, n, k, b_transposed, opt)
         return
-    tol = 1e-12 if name == "float64" else gemm_tolerance(name, k)
+    tol = 1e-12 if name == "float64" else GEMM_TOLERANCE[name]
     err = oracle.rel_to_max_error(got, ref)
     assert err <= tol, (name, m, n, k, b_transposed, opt, err)

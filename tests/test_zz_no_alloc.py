@@ -1,15 +1,20 @@
 """The no-allocation GEMM entry point, through the C ABI.
 
 trb_gemm_launch_noalloc is for callers that cannot let a library allocate
-device memory (a framework whose allocator already owns most of HBM, or a
-latency-critical path that cannot absorb cudaMalloc's synchronisation).  Its
-split-K scratch lives in a fixed array inside the library, so these checks:
-  * compare it with the ordinary entry point (trb_gemm_launch_ex, same
-    kernel, same split count) within the GEMM tolerances of the other tests,
-    on two calls in a row -- the array keeps the previous call's contents,
-    and the second call must not see stale counters or partials;
-  * check that a request larger than the fixed scratch is refused with a
-    clear error.
+device memory: a framework whose caching allocator already holds nearly all of
+HBM (a library cudaMalloc would fail there, or fragment memory the framework
+manages), or a latency-critical path that cannot absorb the synchronisation
+cudaMalloc / cudaFree may imply.  Its split-K scratch lives in one fixed array
+inside the library, shared by every call, so these checks:
+  * call it twice in a row on DIFFERENT operands: the first call leaves its
+    partials and counters in the array, and the second must not read them.
+    Each result must be bit-identical to the ordinary entry point
+    (trb_gemm_launch_ex, single-CTA 128 x 256 kernel, same split count: the
+    same kernel and the same summation order) and within the GEMM tolerance
+    of the fp64 CPU oracle (int8 exact);
+  * with splits = 0, pick a split count that fits the array instead of
+    refusing the call;
+  * refuse an explicit split count larger than the array with a clear error.
 This file sorts last so that a run stopping at the first failure has already
 run every other test; it also passes alone in a fresh process."""
 from __future__ import annotations
@@ -17,7 +22,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from tests.helpers import GEMM_OUT, GEMM_TOLERANCE, gemm_operands, gemm_result_f64, torch_dtype
+from tests.helpers import GEMM_OUT, GEMM_TOLERANCE, gemm_operands, gemm_result_f64, to_raw, torch_dtype
 
 pytestmark = pytest.mark.gpu
 
@@ -51,27 +56,50 @@ def _noalloc(name, a, b, sa, sb, splits):
     return c
 
 
+def _check_oracle(name, a, b, sa, sb, c):
+    m = a.shape[0]
+    rows = np.arange(m) if m <= 128 else np.sort(np.random.default_rng(0).choice(m, 64, replace=False))
+    ref = oracle.gemm_rows(name, to_raw(a), to_raw(b), rows, sa, sb)
+    got = gemm_result_f64(name, c)[rows]
+    if name == "int8":
+        assert np.array_equal(got.astype(np.int64), ref.astype(np.int64))
+    else:
+        err = oracle.rel_to_max_error(got, ref)
+        assert err <= GEMM_TOLERANCE[name], (name, err)
+
+
 @pytest.mark.parametrize("name,shape,splits", [
-    ("bfloat16", (16, 8192, 8192), 0),      # BASELINE skinny shape, automatic splits
+    ("bfloat16", (16, 8192, 8192), 0),      # BASELINE skinny shape, automatic splits (4, as trb_gemm_launch_ex)
     ("bfloat16", (128, 4096, 4096), 4),
+    ("float16", (96, 2048, 2048), 2),
     ("float8_e4m3fn", (100, 2048, 3072), 3),
     ("int8", (64, 1024, 2048), 5),
     ("tfloat32", (128, 512, 1024), 2),
 ])
-def test_noalloc_matches_existing_entry_point_twice(name, shape, splits):
+def test_noalloc_two_calls_match_existing_entry_point_and_oracle(name, shape, splits):
     m, n, k = shape
-    a, b, sa, sb = gemm_operands(name, m, n, k, seed=m + n + k)
-    want = gemm_result_f64(name, _existing(name, a, b, sa, sb, splits))
-    for _ in range(2):  # second call reuses the array as the first call left it
-        got = gemm_result_f64(name, _noalloc(name, a, b, sa, sb, splits))
-        if name == "int8":
-            assert np.array_equal(got, want)
-        else:
-            assert oracle.rel_to_max_error(got, want) <= GEMM_TOLERANCE[name]
+    for seed in (m + n + k, m + n + k + 1):  # the second call runs on different operands
+        a, b, sa, sb = gemm_operands(name, m, n, k, seed=seed)
+        got = _noalloc(name, a, b, sa, sb, splits)
+        want = _existing(name, a, b, sa, sb, splits)
+        assert torch.equal(got, want), (name, seed)
+        _check_oracle(name, a, b, sa, sb, got)
     assert _native.device_error(0, clear=True) == 0
 
 
-def test_noalloc_rejects_requests_beyond_the_fixed_scratch():
+def test_noalloc_automatic_splits_fit_the_scratch():
+    """36 tiles of 128 x 256: trb_gemm_launch_ex's automatic count (4) would
+    need 144 tile-splits; splits = 0 must lower it to what the array holds
+    (128) and run, not refuse."""
+    name, (m, n, k) = "bfloat16", (128, 9216, 8192)
+    for seed in (3, 4):
+        a, b, sa, sb = gemm_operands(name, m, n, k, seed=seed)
+        c = _noalloc(name, a, b, sa, sb, 0)
+        _check_oracle(name, a, b, sa, sb, c)
+    assert _native.device_error(0, clear=True) == 0
+
+
+def test_noalloc_rejects_explicit_splits_beyond_the_fixed_scratch():
     a = torch.zeros((512, 4096), device="cuda", dtype=torch.bfloat16)
     b = torch.zeros((4096, 8192), device="cuda", dtype=torch.bfloat16)
     c = torch.empty((512, 8192), device="cuda", dtype=torch.bfloat16)
