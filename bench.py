@@ -63,14 +63,17 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def load_traffic(kernel_key: str) -> float | None:
-    """DRAM bytes per algorithmic byte for a kernel, from the committed ncu summary."""
+def load_traffic(kernel_key: str) -> dict | None:
+    """DRAM traffic of one full-size launch of a kernel, from the committed ncu
+    capture (profiles/ncu_traffic.json)."""
     path = ROOT / "profiles" / "ncu_traffic.json"
     if not path.exists():
         return None
     try:
-        data = json.loads(path.read_text())
-        return float(data[kernel_key]["dram_bytes_per_algorithmic_byte"])
+        data = json.loads(path.read_text())[kernel_key]
+        return {k: data[k] for k in ("traffic_bytes_per_launch", "dram_read_bytes_per_launch",
+                                     "dram_write_bytes_at_kernel_end", "written_back_after_kernel_end_bytes",
+                                     "elements", "traffic_rule")}
     except (OSError, ValueError, KeyError, TypeError):
         return None
 
@@ -264,11 +267,15 @@ def run_b200(args) -> None:
     peaks, peak_source = load_peaks()
     per_launch_s = local_s / max(args.steps, 1)
     achieved = BYTES_PER_STEP / per_launch_s / 1e9
-    ratio = load_traffic("hbm_triad_float32")
+    cap = load_traffic("hbm_triad_float32")
+    same_size = cap is not None and cap["elements"] == N_ELEMS
     roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": f"{peak_source} (STREAM copy)",
-                "traffic": round(ratio * BYTES_PER_STEP) if ratio else None,
-                "algorithmic_bytes_per_launch": BYTES_PER_STEP}
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": f"{peak_source} (STREAM copy, burst)",
+                "traffic": cap["traffic_bytes_per_launch"] if same_size else None,
+                "algorithmic_bytes_per_launch": BYTES_PER_STEP,
+                "traffic_detail": ({k: cap[k] for k in ("dram_read_bytes_per_launch", "dram_write_bytes_at_kernel_end",
+                                                        "written_back_after_kernel_end_bytes", "traffic_rule")}
+                                   if same_size else None)}
     value = world * BYTES_PER_STEP * args.steps / max_s / 1e9
 
     # ---- e2e: the same triad through the C-ABI host entry point (pinned host
@@ -365,15 +372,19 @@ def e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e_value, h2d_step
     h2d_gbps = world * nbytes / t_h2d / 1e9
     d2h_gbps = world * nbytes / t_d2h / 1e9
     both_each_gbps = world * nbytes / t_both / 1e9  # each direction, both running
-    step_s = max(h2d_step, d2h_step) * world / 1e9 / both_each_gbps
+    # A step cannot beat any of: its H2D bytes at the H2D rate, its D2H bytes
+    # at the D2H rate, or all its copied bytes at the combined rate seen when
+    # both directions run at once (shared host memory and PCIe).
+    step_s = world * max(h2d_step / (h2d_gbps * 1e9), d2h_step / (d2h_gbps * 1e9),
+                         (h2d_step + d2h_step) / (2 * both_each_gbps * 1e9))
     limit = world * BYTES_PER_STEP / step_s / 1e9
     del h_in, h_out, d_in, d_out
     torch.cuda.empty_cache()
     return {"bound": "pcie (pinned host copies, all ranks at once)", "limit_gbps": round(limit, 2),
             "frac": round(e2e_value / limit, 4), "h2d_gbps": round(h2d_gbps, 2), "d2h_gbps": round(d2h_gbps, 2),
             "h2d_and_d2h_concurrent_gbps_each": round(both_each_gbps, 2),
-            "how": "1 GiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / "
-                   "(max(h2d, d2h) step bytes / concurrent per-direction rate)"}
+            "how": "1 GiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / max(h2d bytes "
+                   "/ h2d rate, d2h bytes / d2h rate, all copied bytes / combined rate of both directions at once)"}
 
 
 def gemm_replicas(torch, dev, stream, barrier, max_over_ranks, world, local, dist) -> dict:
