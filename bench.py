@@ -335,11 +335,11 @@ def run_b200(args) -> None:
 def e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e_value, h2d_step, d2h_step) -> dict:
     """What bounds `e2e`: pinned host<->device copies, measured on every rank at
     once (1 GiB with cudaMemcpyAsync: H2D alone, D2H alone, and both directions
-    together on two streams).  A step moves h2d_step bytes in and d2h_step out,
-    which can overlap, so the fastest possible step takes the longer of the
-    two directions at their concurrent rates; the limit is the triad's
-    algorithmic bytes over that time, for all ranks together.  All ranks share
-    the host's DRAM, which also caps these copies."""
+    together on two streams).  A step moves h2d_step bytes in and d2h_step out;
+    it cannot be faster than its H2D bytes at the H2D-alone rate, so the limit
+    is the triad's algorithmic bytes over that time, for all ranks together.
+    All ranks share the host's DRAM and PCIe root, which also caps these
+    copies as N grows."""
     nbytes = 1 << 30
     h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
@@ -372,19 +372,18 @@ def e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e_value, h2d_step
     h2d_gbps = world * nbytes / t_h2d / 1e9
     d2h_gbps = world * nbytes / t_d2h / 1e9
     both_each_gbps = world * nbytes / t_both / 1e9  # each direction, both running
-    # A step cannot beat any of: its H2D bytes at the H2D rate, its D2H bytes
-    # at the D2H rate, or all its copied bytes at the combined rate seen when
-    # both directions run at once (shared host memory and PCIe).
-    step_s = world * max(h2d_step / (h2d_gbps * 1e9), d2h_step / (d2h_gbps * 1e9),
-                         (h2d_step + d2h_step) / (2 * both_each_gbps * 1e9))
+    # A step cannot be faster than bringing its inputs in at the rate the
+    # host-to-device copies reach on their own.  Its D2H copies overlap them
+    # but compete for host memory and PCIe, which is why e2e sits below this.
+    step_s = world * h2d_step / (h2d_gbps * 1e9)
     limit = world * BYTES_PER_STEP / step_s / 1e9
     del h_in, h_out, d_in, d_out
     torch.cuda.empty_cache()
     return {"bound": "pcie (pinned host copies, all ranks at once)", "limit_gbps": round(limit, 2),
             "frac": round(e2e_value / limit, 4), "h2d_gbps": round(h2d_gbps, 2), "d2h_gbps": round(d2h_gbps, 2),
             "h2d_and_d2h_concurrent_gbps_each": round(both_each_gbps, 2),
-            "how": "1 GiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / max(h2d bytes "
-                   "/ h2d rate, d2h bytes / d2h rate, all copied bytes / combined rate of both directions at once)"}
+            "how": "1 GiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / (h2d bytes / "
+                   "h2d-alone rate); the d2h and both-at-once rates are context"}
 
 
 def gemm_replicas(torch, dev, stream, barrier, max_over_ranks, world, local, dist) -> dict:
