@@ -334,13 +334,13 @@ def run_b200(args) -> None:
 
 def e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e_value, h2d_step, d2h_step) -> dict:
     """What bounds `e2e`: pinned host<->device copies, measured on every rank at
-    once (1 GiB with cudaMemcpyAsync: H2D alone, D2H alone, and both directions
+    once (512 MiB with cudaMemcpyAsync: H2D alone, D2H alone, and both directions
     together on two streams).  A step moves h2d_step bytes in and d2h_step out;
     it cannot be faster than its H2D bytes at the H2D-alone rate, so the limit
     is the triad's algorithmic bytes over that time, for all ranks together.
     All ranks share the host's DRAM and PCIe root, which also caps these
     copies as N grows."""
-    nbytes = 1 << 30
+    nbytes = 1 << 29  # 512 MiB per direction: every rank already holds 12 GiB pinned for e2e
     h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     d_in = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -382,7 +382,7 @@ def e2e_roofline(torch, dev, barrier, max_over_ranks, world, e2e_value, h2d_step
     return {"bound": "pcie (pinned host copies, all ranks at once)", "limit_gbps": round(limit, 2),
             "frac": round(e2e_value / limit, 4), "h2d_gbps": round(h2d_gbps, 2), "d2h_gbps": round(d2h_gbps, 2),
             "h2d_and_d2h_concurrent_gbps_each": round(both_each_gbps, 2),
-            "how": "1 GiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / (h2d bytes / "
+            "how": "512 MiB cudaMemcpyAsync per direction, max over ranks; limit = triad bytes / (h2d bytes / "
                    "h2d-alone rate); the d2h and both-at-once rates are context"}
 
 
