@@ -550,27 +550,29 @@ extern "C" int trb_selftest_bounded_wait(uint32_t limit_us, int device_id, trb_r
     fill_result_common(out, device_id);
     // Words left by earlier calls would be reported as this probe's.
     if (hbm::read_error(true) < 0 || gemm::read_error(true) < 0) return TRB_ERR_CUDA;
-    cudaStream_t s = nullptr;
-    cudaEvent_t start = nullptr, stop = nullptr;
-    TRB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-    TRB_CUDA(cudaEventCreate(&start));
-    TRB_CUDA(cudaEventCreate(&stop));
-    TRB_CUDA(cudaEventRecord(start, s));
-    rc = gemm::wait_probe((uint64_t)limit_us * 1000ull, s);
-    if (rc == TRB_OK) {
-        TRB_CUDA(cudaEventRecord(stop, s));
-        TRB_CUDA(cudaEventSynchronize(stop));
-        float ms = 0.f;
-        TRB_CUDA(cudaEventElapsedTime(&ms, start, stop));
-        out->elapsed_s = ms / 1000.0;
-        out->grid = 1;
-        out->block = 64;
-        out->launches = 1;
-        snprintf(out->implementation, sizeof(out->implementation), "bounded_wait_probe");
-    }
-    cudaEventDestroy(start);
-    cudaEventDestroy(stop);
-    cudaStreamDestroy(s);
+    struct Handles {  // released on every return path
+        cudaStream_t s = nullptr;
+        cudaEvent_t start = nullptr, stop = nullptr;
+        ~Handles() {
+            if (start) cudaEventDestroy(start);
+            if (stop) cudaEventDestroy(stop);
+            if (s) cudaStreamDestroy(s);
+        }
+    } h;
+    TRB_CUDA(cudaStreamCreateWithFlags(&h.s, cudaStreamNonBlocking));
+    TRB_CUDA(cudaEventCreate(&h.start));
+    TRB_CUDA(cudaEventCreate(&h.stop));
+    TRB_CUDA(cudaEventRecord(h.start, h.s));
+    rc = gemm::wait_probe((uint64_t)limit_us * 1000ull, h.s);
     if (rc != TRB_OK) return rc;
+    TRB_CUDA(cudaEventRecord(h.stop, h.s));
+    TRB_CUDA(cudaEventSynchronize(h.stop));
+    float ms = 0.f;
+    TRB_CUDA(cudaEventElapsedTime(&ms, h.start, h.stop));
+    out->elapsed_s = ms / 1000.0;
+    out->grid = 1;
+    out->block = 64;
+    out->launches = 1;
+    snprintf(out->implementation, sizeof(out->implementation), "bounded_wait_probe");
     return check_device_errors(out);
 }
