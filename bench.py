@@ -15,6 +15,7 @@ Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -422,15 +423,11 @@ def gemm_replicas(torch, dev, stream, barrier, max_over_ranks, world, local, dis
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             barrier()
             torch.cuda.synchronize(dev)
-            sampler = ClockSampler(local) if sample else None
-            if sampler:
-                sampler.__enter__()
-            e0.record(stream)
-            run(iters)
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-            if sampler:
-                sampler.__exit__(None, None, None)
+            with (ClockSampler(local) if sample else contextlib.nullcontext()) as sampler:
+                e0.record(stream)
+                run(iters)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
             barrier()
             return max_over_ranks(e0.elapsed_time(e1) / 1e3), (sampler.summary() if sampler else None)
 
