@@ -176,6 +176,9 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     const int local = tile - g * group;
     mb = first_m + local % gm;
     nb = local / gm;
+    // Serpentine: odd groups walk the columns backwards, so the first tiles of a
+    // group reuse the B panels the previous group's last tiles left in L2.
+    if (g & 1) nb = num_n - 1 - nb;
 }
 
 // Output element bytes: bf16 for bf16 / e4m3 inputs, f16 for f16, f32 for
