@@ -66,3 +66,31 @@ def test_launcher_reports_skipped_json_on_bad_input():
 
         payload = json.loads(done.stdout.strip().splitlines()[-1])
         assert payload["status"] == "skipped" and payload["error"]
+
+
+_MFU_SHAPE = ["--dtype", "bfloat16", "--m", "64", "--n", "64", "--k", "64"]
+
+
+@pytest.mark.parametrize("exe_name, args, error", [
+    # mfu_gemm_common.hip.hpp:92-104: unknown keys, non-positive sizes, negative counts
+    ("mfu", ["--dtype", "bfloat16", "--m", "0", "--n", "64", "--k", "64"], "matrix dimensions must be positive"),
+    ("mfu", ["--dtype", "bfloat16", "--m", "64", "--n", "-1", "--k", "64"], "matrix dimensions must be positive"),
+    ("mfu", _MFU_SHAPE + ["--warmup", "-1"], "warmup and iterations must be non-negative"),
+    ("mfu", _MFU_SHAPE + ["--iterations", "-1"], "warmup and iterations must be non-negative"),
+    ("mfu", _MFU_SHAPE + ["--blocks-per-cu", "-1"], "blocks-per-cu must be non-negative"),
+    ("mfu", _MFU_SHAPE + ["--bogus", "1"], "unknown argument --bogus"),
+    # hbm_bandwidth.hip.cpp:139-162: unknown keys and missing values
+    ("hbm", ["--dtype", "float32", "--mode", "triad", "--bogus", "1"], "unknown argument --bogus"),
+    ("hbm", ["--dtype", "float32", "--mode", "triad", "--warmup"], "missing value for argument --warmup"),
+    # an addition: the reference parses --size-mib 0 and goes on to an empty launch
+    ("hbm", ["--dtype", "float32", "--mode", "triad", "--size-mib", "0"], "size-mib must be positive"),
+])
+def test_launcher_argument_errors_match_reference(exe_name, args, error):
+    """Rejected argv gives the reference's skipped record and message, exit 0, no device work."""
+    import json
+
+    exe = _native.MFU_EXECUTABLE if exe_name == "mfu" else _native.HBM_EXECUTABLE
+    done = subprocess.run([str(exe), *args], capture_output=True, text=True, timeout=60)
+    assert done.returncode == 0
+    payload = json.loads(done.stdout.strip().splitlines()[-1])
+    assert payload == {"status": "skipped", "error": error}
