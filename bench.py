@@ -152,8 +152,30 @@ def cpu_baseline_leg(torch_module) -> dict:
         if time.perf_counter() - t0 > 5.0 or reps >= 40:
             break
     elapsed = (time.perf_counter() - t0) / reps
+    del b, c, out
     return {"value": round(3 * n * 4 / elapsed / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"float32 triad over 2^28 elements (3.2 GB per pass), {reps} passes, oracle/trb_oracle.c"}
+            "sample": f"float32 triad over 2^28 elements (3.2 GB per pass), {reps} passes, oracle/trb_oracle.c",
+            "gemm": cpu_gemm_baseline(torch_module)}
+
+
+def cpu_gemm_baseline(torch_module) -> dict:
+    """The reference's torch-CPU GEMM case (bf16 torch.mm, mfu.py:230-252) on this
+    host's cores, beside the kernels' bf16 figures: a bounded sample of one
+    warm-up and two or three timed calls per size (about 3 s in all)."""
+    from oracle import reference_cpu
+
+    prev = torch_module.get_num_threads()
+    torch_module.set_num_threads(host_threads())
+    out = {"kind": "reference torch.mm restated (oracle/reference_cpu.py)", "unit": "TFLOP/s",
+           "cpu_capability": torch_module.backends.cpu.get_cpu_capability()}
+    try:
+        for size, iters in ((4096, 3), (8192, 2)):
+            r = reference_cpu.time_gemm(torch_module, "bfloat16", size, size, size, 1, iters)
+            out[f"bfloat16_{size}"] = {"value": round(r["tflops"], 3), "elapsed_s": round(r["elapsed_s"], 4),
+                                       "cores": r["threads"], "sample": f"1 warm-up + {iters} timed calls"}
+    finally:
+        torch_module.set_num_threads(prev)
+    return out
 
 
 def host_threads() -> int:

@@ -18,6 +18,7 @@ way to time the reference's arithmetic on host cores.
 """
 from __future__ import annotations
 
+import math
 import time
 from typing import Callable
 
@@ -63,3 +64,26 @@ def time_hbm(torch, mode: str, n: int, dtype_name: str, scale: float, warmup: in
     moved = factor * n * b.element_size()
     return {"elapsed_s": elapsed, "moved_bytes": moved, "gbps": moved / elapsed / 1e9,
             "threads": torch.get_num_threads()}
+
+
+def gemm_inputs(torch, m: int, n: int, k: int, dtype_name: str, seed: int = 0):
+    """BASELINE GEMM inputs: A (m x k) then B (k x n) ~ N(0, 1)/sqrt(k) from `seed`
+    (CPU generator), cast to the dtype.  The reference draws unseeded randn
+    (utils.py:32-48); the scale keeps bf16 products in range at every K."""
+    g = torch.Generator().manual_seed(seed)
+    dt = getattr(torch, dtype_name)
+    a = torch.randn((m, k), generator=g) / math.sqrt(k)
+    b = torch.randn((k, n), generator=g) / math.sqrt(k)
+    return a.to(dt), b.to(dt)
+
+
+def time_gemm(torch, dtype_name: str, m: int, n: int, k: int, warmup: int, iterations: int) -> dict:
+    """The reference's torch GEMM case (mfu.py:230-240): torch.mm(a, b, out=out)
+    with out in the input dtype, timed by timed_iterations; achieved_ops = 2mnk
+    (mfu.py:252)."""
+    a, b = gemm_inputs(torch, m, n, k, dtype_name)
+    out = torch.empty((m, n), dtype=a.dtype)
+    elapsed = timed_iterations(lambda: torch.mm(a, b, out=out), warmup, iterations)
+    ops = 2 * m * n * k
+    return {"elapsed_s": elapsed, "achieved_ops": ops, "tflops": ops / elapsed / 1e12,
+            "threads": torch.get_num_threads(), "warmup": warmup, "iterations": iterations}
