@@ -121,7 +121,8 @@ typedef struct trb_gemm_args {
 typedef struct trb_gemm_options {
     int32_t splits;          /* 0 = automatic split-K; >= 1 forces that many K splits (global workspace);
                                 -2 / -4 / -8 = that many splits reduced inside a thread-block cluster */
-    int32_t cta_pair;        /* < 0 automatic, 0 = single-CTA 128 x 256 tiles, > 0 = CTA-pair 256 x 256 tiles */
+    int32_t cta_pair;        /* < 0 automatic, 0 = single-CTA 128 x 256 tiles, 2 = CTA pair with 256 x 512 tiles
+                                (bf16 / f16 / e4m3, whole tiles), other > 0 = CTA-pair 256 x 256 tiles */
     int32_t b_layout;        /* trb_b_layout */
     int32_t tile_n;          /* 0 = automatic; 64, 128 or 256 = single-CTA kernel with tiles of that width;
                                 < 0 = swapped-operand kernel (C^T = B^T A^T, m <= 64) */
@@ -209,6 +210,10 @@ int trb_gemm_launch(int dtype, int m, int n, int k, const void* a, const void* b
  *            kernel (C^T = B^T A^T: 128 columns of C per tile, the rows of A as
  *            the MMA's N = 16, 32 or 64), and M <= 128 with few tiles takes
  *            narrow single-CTA tiles (128 x 64; 128 x 128 for 8-bit row-major B).
+ *            cta_pair = 2 runs the CTA pair with 256 x 512 tiles (one A load
+ *            per k-block feeds two MMAs: 25% fewer L2 -> SM bytes per FLOP) for
+ *            bf16, f16 and e4m3 inputs without split-K; its results are
+ *            bit-identical to the 256 x 256 pair's.
  *  b_layout: TRB_B_K_MAJOR reads b as B^T (row-major N x K).
  *  tile_n:   0 automatic; 64 / 128 / 256 force the single-CTA kernel with that
  *            tile width (8-bit row-major B: >= 128); < 0 forces the

@@ -1659,6 +1659,304 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------ wide CTA-pair kernel
+// The CTA pair with 256 x 512 tiles: each k-block's A rows feed two
+// cta_group::2 MMAs (N = 256 each: tile columns [0, 256) and [256, 512)) into
+// one 512-column accumulator per CTA, all of its TMEM.  Each SM then pulls
+// 48 KiB from L2 per 128 x 512 x 128-byte step instead of 2 x 32 KiB: 25%
+// fewer L2 -> SM bytes per FLOP, without multicast.  With no second
+// accumulator the next tile waits until the epilogue has read this one out, so
+// eight epilogue warps (two per TMEM lane quarter, 128 columns of each half
+// apiece) copy it into registers as packed 16-bit results, release TMEM at
+// once, and stage / store from registers while the next tile runs.  The two
+// halves are completed, read out and released one after the other: half 0's
+// read-out and the next tile's first half-0 MMAs overlap half 1.  16-bit
+// outputs only (bf16, f16, e4m3 -> bf16): 32-bit ones would not fit in
+// registers.  Every accumulator sums its k-blocks in increasing order with the
+// pair kernel's instructions, so the two agree bit for bit.  Whole tiles only.
+constexpr int kWideN = 2 * kPairN;              // cols per wide tile
+constexpr int kWideStages = 4;
+constexpr int kWideBStage = 2 * kPairBStage;    // 32 KiB: this CTA's B columns of both halves
+constexpr size_t kWideRingBytes = (size_t)kWideStages * (kPairAStage + kWideBStage);
+constexpr int kWideEpiWarps = 8;
+constexpr int kWideThreads = 64 + 32 * kWideEpiWarps;  // producer, MMA issuer, 8 epilogue warps
+template <int DT>
+__host__ __device__ constexpr size_t wide_smem_bytes() {
+    return kWideRingBytes + 1024 + (size_t)kWideEpiWarps * 2 * epi_box_bytes<DT>();
+}
+
+// Two fp32 accumulator words -> one word of packed bf16 / f16 (convert16's rounding).
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(uint32_t r0, uint32_t r1, float out_scale) {
+    float lo = __uint_as_float(r0), hi = __uint_as_float(r1);
+    if constexpr (DT == TRB_FLOAT8_E4M3FN) {
+        lo *= out_scale;
+        hi *= out_scale;
+    }
+    if constexpr (DT == TRB_FLOAT16) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+
+// Row `row` of a 16-bit staging box from 16 packed words (the layout of stage_row).
+__device__ __forceinline__ void stage_row_packed(uint32_t buf, int row, const uint32_t (&w)[16]) {
+    const uint32_t base = buf + (uint32_t)(row * 64);
+    const int sw = (row >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        st_shared_v4(base + (uint32_t)((j ^ sw) * 16), w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+
+template <int DT, bool KB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
+    gemm_tcgen05_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmC, int M, int N, int K, float out_scale,
+                             int group_m) {
+    using Tr = Traits<DT>;
+    constexpr int kBKElems = kBKBytes / Tr::kEsize;
+    constexpr int kBoxN = 128 / Tr::kEsize;
+    constexpr int kBBoxes = kHalfN / kBoxN;                 // B boxes per CTA per half per stage
+    constexpr int kBBoxBytes = kBKElems * 128;
+    constexpr int kInstrKRows = kInstrKBytes / Tr::kEsize;
+    constexpr uint32_t kIdesc = KB ? idesc_b_kmajor(make_idesc_pair(Tr::kIdesc)) : make_idesc_pair(Tr::kIdesc);
+    static_assert(out_esize<DT>() == 2, "the wide pair holds 16-bit results in registers");
+    static_assert(wide_smem_bytes<DT>() <= 227 * 1024, "wide pair shared memory");
+
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kWideStages];   // leader: both CTAs' TMA bytes land here
+    __shared__ __align__(8) uint64_t empty_bar[kWideStages];  // both: MMA finished reading the stage
+    __shared__ __align__(8) uint64_t accf_bar[2];             // both: the tile's half h is complete
+    __shared__ __align__(8) uint64_t acce_bar[2];             // leader: both CTAs' epilogues read half h out
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+
+    const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    const uint32_t sA = smem_base;
+    const uint32_t sB = smem_base + kWideStages * kPairAStage;
+    const uint32_t sEpi = smem_base + (uint32_t)kWideRingBytes;  // TMA-store staging, 1 KiB aligned
+
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int pair = blockIdx.x >> 1;
+    const int num_pairs = gridDim.x >> 1;
+    const int num_m = (M + kPairM - 1) / kPairM;
+    const int num_n = (N + kWideN - 1) / kWideN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + kBKElems - 1) / kBKElems;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWideStages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(smem_u32(&accf_bar[h]), 1);
+            mbar_init(smem_u32(&acce_bar[h]), 2 * kWideEpiWarps);  // 8 epilogue warps x 2 CTAs
+        }
+        mbar_init(smem_u32(&drain_bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmC);
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(smem_u32(&tmem_slot), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // barrier inits of both CTAs visible before any cross-CTA signal
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_slot;
+    grid_launch_dependents();  // the next grid may set up; its global accesses wait for this one
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs; completion on the leader's full barriers)
+            grid_dependency_wait();  // A and B may be outputs of the previous grid
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;
+            bool ok = true;
+            for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
+                int mb, nb;
+                tile_coords(tile, num_m, num_n, group_m, mb, nb);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(smem_u32(&empty_bar[stage]), phase ^ 1u, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrProducerWait);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb_local = smem_u32(&full_bar[stage]);
+                    if (leader) mbar_arrive_expect_tx(fb_local, 2 * (kPairAStage + kWideBStage));
+                    const uint32_t fb = fb_local & kPeerBitMask;
+                    tma_load_2d_pair(sA + stage * kPairAStage, &tmA, fb, kb * kBKElems, mb * kPairM + rank * kBM);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t dst = sB + stage * kWideBStage + h * kPairBStage;
+                        const int col0 = nb * kWideN + h * kPairN + (int)rank * kHalfN;
+                        if constexpr (KB) {
+                            tma_load_2d_pair(dst, &tmB, fb, kb * kBKElems, col0);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < kBBoxes; ++j)
+                                tma_load_2d_pair(dst + j * kBBoxBytes, &tmB, fb, col0 + j * kBoxN, kb * kBKElems);
+                        }
+                    }
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kWideStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (leader)  // every armed phase completes only once both CTAs' bytes have landed
+                for (int s = 0; s < kWideStages; ++s)
+                    if (issued_mask & (1u << s))
+                        if (!mbar_wait_cluster(smem_u32(&full_bar[s]), (issued_phase >> s) & 1u, nullptr))
+                            atomicCAS(&g_gemm_error, 0, kErrDrainWait);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer: the leader CTA only
+            const uint64_t a_desc0 = make_sdesc(sA, 16, 1024);
+            const uint64_t b_desc0 = KB ? make_sdesc(sB, 16, 1024)
+                                        : make_sdesc(sB, kBBoxBytes, Tr::BLayout::kSbo, Tr::BLayout::kLayoutType);
+            constexpr int kBKStep = KB ? kInstrKBytes : kInstrKRows * 128;
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            int t_local = 0;
+            for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++t_local) {
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
+                        atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                        abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kPairAStage) >> 4);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        // first k-block: the epilogues have read this half of the previous tile out of TMEM
+                        if (kb == 0) {
+                            if (!mbar_wait_cluster(smem_u32(&acce_bar[h]), ((uint32_t)t_local & 1u) ^ 1u,
+                                                   &abort_flag)) {
+                                atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                                abort_flag = 1;
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kWideBStage + h * kPairBStage) >> 4);
+                        const uint32_t d_tmem = tmem_base + (uint32_t)(h * kPairN);
+#pragma unroll
+                        for (int ks = 0; ks < kKSteps; ++ks)
+                            mma_pair<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kInstrKBytes >> 4),
+                                                b_stage + (uint64_t)(ks * kBKStep >> 4), kIdesc,
+                                                (kb != 0 || ks != 0) ? 1u : 0u);
+                        // last k-block: half h is complete once these MMAs are
+                        if (kb == num_kb - 1) tc_commit_pair_multicast(smem_u32(&accf_bar[h]), 0x3);
+                    }
+                    if (!ok) break;
+                    tc_commit_pair_multicast(smem_u32(&empty_bar[stage]), 0x3);
+                    if (++stage == kWideStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            tc_commit_pair_multicast(smem_u32(&drain_bar), 0x1);
+            if (!mbar_wait_cluster(smem_u32(&drain_bar), 0, nullptr)) atomicCAS(&g_gemm_error, 0, kErrDrainWait);
+        }
+    } else {
+        // ---------------- epilogue (both CTAs): warps 2..9; warp w reads TMEM lanes
+        // [32 (w % 4), +32) -- this CTA's accumulator rows -- in columns [128 cb, +128) of each
+        // half, cb = (w - 2) / 4: 8 boxes of 32 x 32 results per tile
+        grid_dependency_wait();  // C may be in use by the previous grid
+        const int q = warp & 3;
+        const int ew = warp - 2;
+        const int cb = ew >> 2;
+        const uint32_t acce_leader0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
+        const uint32_t acce_leader1 = mapa_shared(smem_u32(&acce_bar[1]), 0);
+        const uint32_t t_rows = tmem_base + ((uint32_t)(q * 32) << 16);
+        uint32_t boxes = 0;  // TMA-store boxes this warp has issued (selects its staging buffer)
+        int t_local = 0;
+        for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t_local) {
+            int mb, nb;
+            tile_coords(tile, num_m, num_n, group_m, mb, nb);
+            uint32_t w[8][16];  // box i: half i / 4, columns 128 cb + 32 (i % 4) of that half
+            bool ok = true;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                ok = mbar_wait_cluster(smem_u32(&accf_bar[h]), (uint32_t)t_local & 1u, &abort_flag);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int i = 4 * h; i < 4 * h + 4; ++i) {
+#pragma unroll
+                    for (int p = 0; p < 2; ++p) {  // 16 columns at a time keeps the kernel within its registers
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(t_rows + (uint32_t)(h * kPairN + cb * 128 + (i & 3) * 32 + p * 16), r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) w[i][p * 8 + j] = pack2<DT>(r[2 * j], r[2 * j + 1], out_scale);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(h ? acce_leader1 : acce_leader0);  // half h of TMEM is free
+            }
+            if (!ok) {
+                if (lane == 0) {
+                    atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
+                    abort_flag = 1;
+                }
+                break;
+            }
+            const int row0 = mb * kPairM + (int)rank * kBM + q * 32;  // first row of this warp's boxes
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int gcol = nb * kWideN + (i >> 2) * kPairN + cb * 128 + (i & 3) * 32;
+                if (row0 >= M || gcol >= N) continue;  // warp-uniform: the box lies outside C
+                const uint32_t buf = sEpi + (uint32_t)((ew * 2 + (int)(boxes & 1u)) * epi_box_bytes<DT>());
+                if (lane == 0) bulk_wait_read<1>();  // the store issued two boxes ago has read `buf`
+                __syncwarp();
+                stage_row_packed(buf, lane, w[i]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmC, buf, gcol, row0);
+                    bulk_commit();
+                }
+                ++boxes;
+            }
+        }
+        if (lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before teardown
+        __syncwarp();
+    }
+
+    // Teardown: the leader's MMAs read the peer's shared memory and write its
+    // TMEM, so neither CTA releases TMEM or exits before both are done.
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1852,7 +2150,8 @@ static int raster_group(int rows_per_block, int k, int es) {
 // waits order their global accesses after the previous grid) and, for
 // cluster split-K, the cluster shape.
 template <typename Kernel, typename... Args>
-static int launch_ex(Kernel kernel, int grid, size_t smem, int cluster, cudaStream_t stream, Args... args) {
+static int launch_ex_threads(Kernel kernel, int grid, int threads, size_t smem, int cluster, cudaStream_t stream,
+                             Args... args) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     int nattr = 0;
@@ -1867,13 +2166,18 @@ static int launch_ex(Kernel kernel, int grid, size_t smem, int cluster, cudaStre
         ++nattr;
     }
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3((unsigned)threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
     TRB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...));
     return TRB_OK;
+}
+
+template <typename Kernel, typename... Args>
+static int launch_ex(Kernel kernel, int grid, size_t smem, int cluster, cudaStream_t stream, Args... args) {
+    return launch_ex_threads(kernel, grid, kThreads, smem, cluster, stream, args...);
 }
 
 template <int DT, bool KB, int BN, int CL = 1>
@@ -2097,6 +2401,32 @@ static int launch_swap_kd(int cluster, const void* a, const void* b, int m, int 
     }
 }
 
+// The 256 x 512 CTA pair: whole tiles, one persistent pair per SM pair.
+template <int DT, bool KB>
+static int launch_wide(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, int m, int n, int k,
+                       float out_scale, int group_m, int dev, int sms, cudaStream_t stream, LaunchInfo* info) {
+    static bool attr_set[64] = {};
+    if (dev < 64 && !attr_set[dev]) {
+        TRB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_wide_kernel<DT, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)wide_smem_bytes<DT>()));
+        attr_set[dev] = true;
+    }
+    const long tiles = (long)((m + kPairM - 1) / kPairM) * ((n + kWideN - 1) / kWideN);
+    const int grid_workers = (int)std::max<long>(1, std::min<long>(tiles, sms / 2));
+    const int rc = launch_ex_threads(gemm_tcgen05_wide_kernel<DT, KB>, grid_workers * 2, kWideThreads,
+                                     wide_smem_bytes<DT>(), 1, stream, tmA, tmB, tmC, m, n, k, out_scale, group_m);
+    if (rc != TRB_OK) return rc;
+    TRB_CUDA(cudaGetLastError());
+    if (info) {
+        *info = LaunchInfo{};
+        info->grid = grid_workers * 2;
+        info->block = kWideThreads;
+        info->pair = 1;
+        info->tile_n = kWideN;
+    }
+    return TRB_OK;
+}
+
 template <int DT, bool KB>
 static int launch_typed(int m, int n, int k, const void* a, const void* b, void* c, float out_scale, int splits,
                         int cta_pair, int tile_n_opt, cudaStream_t stream, LaunchInfo* info) {
@@ -2163,6 +2493,11 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     }
     const bool pair = cluster == 1 && (cta_pair > 0 || pair_auto) && sms >= 2;
     const int tile_n = pair ? kPairN : tile_n_single;
+    if (cta_pair == 2 && (!pair || out_esize<DT>() != 2 || splits > 1 || tile_n_opt != 0)) {
+        set_error("trb_gemm_launch: cta_pair = 2 (CTA pair, 256 x 512 tiles) takes whole tiles (splits 0 or 1, "
+                  "tile_n 0) of bf16, f16 or e4m3 inputs");
+        return TRB_ERR_ARGS;
+    }
 
     CUtensorMap tmA, tmB;
     int rc = encode_2d(&tmA, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -2193,6 +2528,11 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
             return launch_single<DT, KB, 128>(tmA, tmB, tmC, m, n, k, c, out_scale, splits, dev, sms, stream, info);
         }
         return launch_single<DT, KB, 256>(tmA, tmB, tmC, m, n, k, c, out_scale, splits, dev, sms, stream, info);
+    }
+    if (cta_pair == 2) {
+        if constexpr (out_esize<DT>() == 2)
+            return launch_wide<DT, KB>(tmA, tmB, tmC, m, n, k, out_scale, raster_group(kPairM, k, es), dev, sms, stream,
+                                       info);
     }
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {

@@ -53,7 +53,8 @@ struct LaunchInfo {
     int cluster = 1;  // > 1: K splits reduced inside a thread-block cluster of that size
 };
 // splits: 0 = automatic (split-K only for problems that leave SMs idle), >= 1 forced.
-// cta_pair: < 0 automatic (pair, or narrow single-CTA tiles when skinny), 0 single-CTA, > 0 CTA pair.
+// cta_pair: < 0 automatic (pair, or narrow single-CTA tiles when skinny), 0 single-CTA, 2 CTA pair with
+// 256 x 512 tiles (16-bit outputs, whole tiles), other > 0 CTA pair.
 // b_kmajor: B is stored N x K (K-major) instead of the row-major K x N matrix.
 // tile_n: 0 automatic; 64 / 128 / 256 force the single-CTA kernel at that tile
 // width; < 0 forces the swapped-operand kernel (m <= 64): -1 with the

@@ -92,7 +92,9 @@ def gemm(a: Any, b: Any, out: Any, *, dtype: str | None = None, scale_a: float =
     splits: 0 = automatic split-K, >= 1 forces that many K splits reduced
     through a global workspace, -2 / -4 / -8 that many splits reduced inside a
     thread-block cluster (distributed shared memory).
-    cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel.
+    cta_pair: -1 automatic, 0 single-CTA 128x256 kernel, 1 CTA-pair 256x256 kernel,
+    2 CTA pair with 256x512 tiles (bf16 / f16 / e4m3 inputs, no split-K; bit-identical
+    to cta_pair=1).
     tile_n: 0 automatic, 64/128/256 single-CTA tile width, -1 the
     swapped-operand skinny kernel (C^T = B^T A^T, m <= 64; automatic for
     m <= 64)."""

@@ -163,6 +163,41 @@ def test_pair_and_single_agree_bitwise_for_int8():
     assert torch.equal(_run("int8", a, b, cta_pair=0), _run("int8", a, b, cta_pair=1))
 
 
+@pytest.mark.parametrize("name", ["bfloat16", "float16", "float8_e4m3fn"])
+@pytest.mark.parametrize("b_transposed", [False, True])
+@pytest.mark.parametrize("shape", [(300, 528, 208), (520, 1104, 1024), (1, 16, 16), (768, 1536, 4096),
+                                   (2048, 4096, 512)])
+def test_wide_pair_kernel_matches_pair_bitwise(name, b_transposed, shape):
+    """cta_pair = 2, the CTA pair with 256 x 512 tiles: each accumulator sums its
+    k-blocks in the pair kernel's order with the same instructions, so the bits
+    agree; ragged M / N / K tails, a tile whose second half lies past N, and
+    several tiles per SM pair (the accumulator handed from tile to tile)."""
+    m, n, k = shape
+    a, b, sa, sb = gemm_operands(name, m, n, k, seed=m + 3 * n)
+    bb = b.t().contiguous() if b_transposed else b
+    outs = []
+    for cta_pair in (1, 2):
+        out = torch.empty((m, n), device="cuda", dtype=torch_dtype(GEMM_OUT[name]))
+        gemm(a, bb, out, dtype=name, scale_a=sa, scale_b=sb, splits=1, cta_pair=cta_pair, b_transposed=b_transposed)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    rows = np.unique(np.linspace(0, m - 1, min(m, 64)).astype(np.int64))
+    _check(name, a, b, outs[1], sa, sb, rows)
+
+
+def test_wide_pair_kernel_option_errors():
+    x = torch.zeros((512, 512), device="cuda", dtype=torch.float32)
+    with pytest.raises(_native.NativeError, match="cta_pair = 2"):  # tf32 folds K chunks: the pair kernel's job
+        gemm(x, x, torch.empty_like(x), dtype="tfloat32", cta_pair=2)
+    y = torch.zeros((512, 512), device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(_native.NativeError, match="cta_pair = 2"):  # whole tiles only
+        gemm(y, y, torch.empty_like(y), splits=2, cta_pair=2)
+    z = torch.zeros((512, 512), device="cuda", dtype=torch.int8)
+    with pytest.raises(_native.NativeError, match="cta_pair = 2"):  # 32-bit results do not fit in registers
+        gemm(z, z, torch.empty((512, 512), device="cuda", dtype=torch.int32), dtype="int8", cta_pair=2)
+
+
 def test_split_k_run_entry_reports_splits():
     res = _native.gemm_run("bfloat16", 16, 1024, 8192, 1, 3)  # 8 swapped panels x clusters of 8 K splits
     assert res.split_k == 8 and res.device_error == 0
