@@ -2498,6 +2498,27 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
                   "tile_n 0) of bf16, f16 or e4m3 inputs");
         return TRB_ERR_ARGS;
     }
+    // Automatic: the 256 x 512 pair replaces a whole-tile 256 x 256 pair for
+    // bf16 / f16 inputs with >= 64 k-blocks when its tiles fill the SM pairs
+    // as well (waves x useful columns).  Measured on B200 against the 256 x 256
+    // pair, each burst after an idle gap: bf16 8192^3 +3.7% (1594 vs 1537
+    // TFLOP/s; cuBLAS 1587), 6144^3 +1.6%, 16384^3 +7%, 4096^3 +0.3%; f16
+    // 8192^3 +4.0%; ~2 s power-capped loops: bf16 8192^3 / 16384^3 +3.7% / +6.8%,
+    // f16 +3.8%.  Not taken for e4m3 (-1.3% / -1.9%: its shorter tiles expose
+    // the accumulator hand-off more) or short K (bf16 8192^2 x 2048: -0.8%).
+    bool wide = cta_pair == 2;
+    if (!wide && pair && pair_auto && splits == 1 && (DT == TRB_BFLOAT16 || DT == TRB_FLOAT16) && num_kb >= 64) {
+        const int workers = sms / 2;
+        auto fill = [workers](long units, long cols, long tile_cols) {  // wave fill x useful share of the columns
+            const long waves = (units + workers - 1) / workers;
+            const long padded = tile_cols * ((cols + tile_cols - 1) / tile_cols);
+            return (double)units / (double)(waves * workers) * (double)cols / (double)padded;
+        };
+        const long mrows = (m + kPairM - 1) / kPairM;
+        const double f_pair = fill(mrows * ((n + kPairN - 1) / kPairN), n, kPairN);
+        const double f_wide = fill(mrows * ((n + kWideN - 1) / kWideN), n, kWideN);
+        wide = f_wide >= f_pair - 0.01;
+    }
 
     CUtensorMap tmA, tmB;
     int rc = encode_2d(&tmA, a, es, (uint64_t)k, (uint64_t)m, kBKBytes / es, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -2529,7 +2550,7 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
         }
         return launch_single<DT, KB, 256>(tmA, tmB, tmC, m, n, k, c, out_scale, splits, dev, sms, stream, info);
     }
-    if (cta_pair == 2) {
+    if (wide) {
         if constexpr (out_esize<DT>() == 2)
             return launch_wide<DT, KB>(tmA, tmB, tmC, m, n, k, out_scale, raster_group(kPairM, k, es), dev, sms, stream,
                                        info);

@@ -207,7 +207,7 @@ def test_split_k_run_entry_reports_splits():
     res = _native.gemm_run("bfloat16", 128, 8192, 8192, 1, 3)  # 64 tiles x clusters of 2 K splits
     assert res.split_k == 2 and res.implementation.decode() == "tcgen05_1cta_128x128_cluster2"
     res = _native.gemm_run("bfloat16", 4096, 4096, 4096, 1, 3)
-    assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x256"
+    assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x512"
     res = _native.gemm_run("float8_e4m3fn", 4096, 4096, 4096, 1, 3)
     assert res.split_k == 1 and res.implementation.decode() == "tcgen05_cta_pair_256x256"
 
@@ -496,12 +496,26 @@ def test_cluster_split_k_option_errors():
 
 @pytest.mark.parametrize("size,impl", [(1024, "tcgen05_1cta_128x64"), (1536, "tcgen05_1cta_128x128"),
                                        (2048, "tcgen05_1cta_128x256"), (3072, "tcgen05_cta_pair_256x256"),
-                                       (8192, "tcgen05_cta_pair_256x256")])
+                                       (8192, "tcgen05_cta_pair_256x512"), (16384, "tcgen05_cta_pair_256x512")])
 def test_automatic_kernel_choice_for_square_sizes(size, impl):
     """The wave model's picks for the BASELINE square sweep (tiles that fill
-    the SMs in whole waves; the pair once the grid is large and K long)."""
+    the SMs in whole waves; the pair once the grid is large; its 256 x 512
+    tiles for bf16 once K reaches 64 k-blocks)."""
     res = _native.gemm_run("bfloat16", size, size, size, 0, 1)
     assert res.implementation.decode() == impl and res.split_k == 1 and res.device_error == 0
+
+
+@pytest.mark.parametrize("name,shape,impl", [("float8_e4m3fn", (8192, 8192, 8192), "tcgen05_cta_pair_256x256"),
+                                             ("bfloat16", (8192, 8192, 2048), "tcgen05_cta_pair_256x256"),
+                                             ("float16", (8192, 8192, 8192), "tcgen05_cta_pair_256x512"),
+                                             ("bfloat16", (8192, 8448, 4096), "tcgen05_cta_pair_256x256")])
+def test_automatic_wide_pair_rule(name, shape, impl):
+    """The 256 x 512 pair is picked for bf16 / f16 with >= 64 k-blocks when its
+    tiles fill the SM pairs as well as 256 x 256 ones; e4m3, short K and a
+    width that wastes part of a 512-wide tile keep the 256 x 256 pair."""
+    m, n, k = shape
+    res = _native.gemm_run(name, m, n, k, 0, 1)
+    assert res.implementation.decode() == impl and res.device_error == 0
 
 
 @pytest.mark.parametrize("shape", [(1024, 1024, 1024), (1536, 1536, 1536), (2048, 2048, 2048)])
