@@ -1668,9 +1668,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // accumulator the next tile waits until the epilogue has read this one out, so
 // eight epilogue warps (two per TMEM lane quarter, 128 columns of each half
 // apiece) copy it into registers as packed 16-bit results, release TMEM at
-// once, and stage / store from registers while the next tile runs.  The two
-// halves are completed, read out and released one after the other: half 0's
-// read-out and the next tile's first half-0 MMAs overlap half 1.  16-bit
+// once, and stage / store from registers while the next tile runs.  16-bit
 // outputs only (bf16, f16, e4m3 -> bf16): 32-bit ones would not fit in
 // registers.  Every accumulator sums its k-blocks in increasing order with the
 // pair kernel's instructions, so the two agree bit for bit.  Whole tiles only.
@@ -1729,8 +1727,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kWideStages];   // leader: both CTAs' TMA bytes land here
     __shared__ __align__(8) uint64_t empty_bar[kWideStages];  // both: MMA finished reading the stage
-    __shared__ __align__(8) uint64_t accf_bar[2];             // both: the tile's half h is complete
-    __shared__ __align__(8) uint64_t acce_bar[2];             // leader: both CTAs' epilogues read half h out
+    __shared__ __align__(8) uint64_t accf_bar;                // both: the tile's accumulator is complete
+    __shared__ __align__(8) uint64_t acce_bar;                // leader: both CTAs' epilogues read it out
     __shared__ __align__(8) uint64_t drain_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
@@ -1756,10 +1754,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), 1);
         }
-        for (int h = 0; h < 2; ++h) {
-            mbar_init(smem_u32(&accf_bar[h]), 1);
-            mbar_init(smem_u32(&acce_bar[h]), 2 * kWideEpiWarps);  // 8 epilogue warps x 2 CTAs
-        }
+        mbar_init(smem_u32(&accf_bar), 1);
+        mbar_init(smem_u32(&acce_bar), 2 * kWideEpiWarps);  // 8 epilogue warps x 2 CTAs
         mbar_init(smem_u32(&drain_bar), 1);
         abort_flag = 0;
         fence_mbar_init();
@@ -1836,6 +1832,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
             bool ok = true;
             int t_local = 0;
             for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++t_local) {
+                // the epilogues have read the previous tile's accumulator out of TMEM
+                if (!mbar_wait_cluster(smem_u32(&acce_bar), ((uint32_t)t_local & 1u) ^ 1u, &abort_flag)) {
+                    atomicCAS(&g_gemm_error, 0, kErrMmaWait);
+                    abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait_cluster(smem_u32(&full_bar[stage]), phase, &abort_flag)) {
                         atomicCAS(&g_gemm_error, 0, kErrMmaWait);
@@ -1846,17 +1849,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                     const uint64_t a_stage = a_desc0 + (uint64_t)((stage * kPairAStage) >> 4);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        // first k-block: the epilogues have read this half of the previous tile out of TMEM
-                        if (kb == 0) {
-                            if (!mbar_wait_cluster(smem_u32(&acce_bar[h]), ((uint32_t)t_local & 1u) ^ 1u,
-                                                   &abort_flag)) {
-                                atomicCAS(&g_gemm_error, 0, kErrMmaWait);
-                                abort_flag = 1;
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                        }
                         const uint64_t b_stage = b_desc0 + (uint64_t)((stage * kWideBStage + h * kPairBStage) >> 4);
                         const uint32_t d_tmem = tmem_base + (uint32_t)(h * kPairN);
 #pragma unroll
@@ -1864,16 +1856,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                             mma_pair<Tr::kKind>(d_tmem, a_stage + (uint64_t)(ks * kInstrKBytes >> 4),
                                                 b_stage + (uint64_t)(ks * kBKStep >> 4), kIdesc,
                                                 (kb != 0 || ks != 0) ? 1u : 0u);
-                        // last k-block: half h is complete once these MMAs are
-                        if (kb == num_kb - 1) tc_commit_pair_multicast(smem_u32(&accf_bar[h]), 0x3);
                     }
-                    if (!ok) break;
                     tc_commit_pair_multicast(smem_u32(&empty_bar[stage]), 0x3);
                     if (++stage == kWideStages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
+                if (ok) tc_commit_pair_multicast(smem_u32(&accf_bar), 0x3);
             }
             tc_commit_pair_multicast(smem_u32(&drain_bar), 0x1);
             if (!mbar_wait_cluster(smem_u32(&drain_bar), 0, nullptr)) atomicCAS(&g_gemm_error, 0, kErrDrainWait);
@@ -1886,37 +1876,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
         const int q = warp & 3;
         const int ew = warp - 2;
         const int cb = ew >> 2;
-        const uint32_t acce_leader0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
-        const uint32_t acce_leader1 = mapa_shared(smem_u32(&acce_bar[1]), 0);
+        const uint32_t acce_leader = mapa_shared(smem_u32(&acce_bar), 0);
         const uint32_t t_rows = tmem_base + ((uint32_t)(q * 32) << 16);
         uint32_t boxes = 0;  // TMA-store boxes this warp has issued (selects its staging buffer)
         int t_local = 0;
         for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t_local) {
             int mb, nb;
             tile_coords(tile, num_m, num_n, group_m, mb, nb);
-            uint32_t w[8][16];  // box i: half i / 4, columns 128 cb + 32 (i % 4) of that half
-            bool ok = true;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                ok = mbar_wait_cluster(smem_u32(&accf_bar[h]), (uint32_t)t_local & 1u, &abort_flag);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                tc_fence_after();
-#pragma unroll
-                for (int i = 4 * h; i < 4 * h + 4; ++i) {
-#pragma unroll
-                    for (int p = 0; p < 2; ++p) {  // 16 columns at a time keeps the kernel within its registers
-                        uint32_t r[16];
-                        tmem_ld_32x32b_x16(t_rows + (uint32_t)(h * kPairN + cb * 128 + (i & 3) * 32 + p * 16), r);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) w[i][p * 8 + j] = pack2<DT>(r[2 * j], r[2 * j + 1], out_scale);
-                    }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(h ? acce_leader1 : acce_leader0);  // half h of TMEM is free
-            }
+            bool ok = mbar_wait_cluster(smem_u32(&accf_bar), (uint32_t)t_local & 1u, &abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0) {
                     atomicCAS(&g_gemm_error, 0, kErrEpilogueWait);
@@ -1924,6 +1892,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
                 }
                 break;
             }
+            tc_fence_after();
+            uint32_t w[8][16];  // box i: half i / 4, columns 128 cb + 32 (i % 4) of that half
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                uint32_t r0[16], r1[16];  // two loads of 16 columns in flight per wait
+                const uint32_t col = (uint32_t)((i >> 2) * kPairN + cb * 128 + (i & 3) * 32);
+                tmem_ld_32x32b_x16(t_rows + col, r0);
+                tmem_ld_32x32b_x16(t_rows + col + 16, r1);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    w[i][j] = pack2<DT>(r0[2 * j], r0[2 * j + 1], out_scale);
+                    w[i][8 + j] = pack2<DT>(r1[2 * j], r1[2 * j + 1], out_scale);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acce_leader);  // TMEM free: the next tile may start
             const int row0 = mb * kPairM + (int)rank * kBM + q * 32;  // first row of this warp's boxes
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -2501,11 +2487,11 @@ static int launch_typed(int m, int n, int k, const void* a, const void* b, void*
     // Automatic: the 256 x 512 pair replaces a whole-tile 256 x 256 pair for
     // bf16 / f16 inputs with >= 64 k-blocks when its tiles fill the SM pairs
     // as well (waves x useful columns).  Measured on B200 against the 256 x 256
-    // pair, each burst after an idle gap: bf16 8192^3 +3.7% (1594 vs 1537
-    // TFLOP/s; cuBLAS 1587), 6144^3 +1.6%, 16384^3 +7%, 4096^3 +0.3%; f16
-    // 8192^3 +4.0%; ~2 s power-capped loops: bf16 8192^3 / 16384^3 +3.7% / +6.8%,
-    // f16 +3.8%.  Not taken for e4m3 (-1.3% / -1.9%: its shorter tiles expose
-    // the accumulator hand-off more) or short K (bf16 8192^2 x 2048: -0.8%).
+    // pair, each burst after an idle gap: bf16 8192^3 +4.2% (1621 vs 1555
+    // TFLOP/s; cuBLAS 1610), 16384^3 +6.6%, 6144^3 +1.6%, 4096^3 +0.4%; f16
+    // 8192^3 +4.8%; ~2 s power-capped loops: bf16 8192^3 +4.1% (1411; cuBLAS
+    // 1390).  Not taken for e4m3 (+0.4% / +0.5%: its tiles are half as long, so
+    // the accumulator hand-off eats the gain) or short K (bf16 8192^2 x 2048: -0.8%).
     bool wide = cta_pair == 2;
     if (!wide && pair && pair_auto && splits == 1 && (DT == TRB_BFLOAT16 || DT == TRB_FLOAT16) && num_kb >= 64) {
         const int workers = sms / 2;
